@@ -1,0 +1,310 @@
+"""Benchmark of the selective-scan hot path on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one selective-scan forward over the configs[1] batch: fp16 u / delta / z / B / C with fp32
+A / D, batch 8, dim 1536, dstate 16, seqlen 4096, D skip, SiLU(z) gate, softplus(delta), final state
+returned. Inputs are seeded synthetic data with the BASELINE distributions (no dataset exists for this
+path). With N > 1 (torchrun, one process per GPU) every rank runs the same per-GPU batch: the scan
+shards by (batch, channel) with no communication, so scaling is weak and the value is the whole-job
+element rate (all ranks' elements / max-over-ranks time).
+
+Printed JSON (rank 0, one line):
+  value       Gelem/s with inputs resident in HBM (CUDA events around K launches, max over ranks)
+  e2e         the same through the public selective_scan API with pinned host inputs: H2D copies of
+              u/delta/z/B/C, the scan, and the D2H read of y and the state inside the timed region
+  roofline    algorithmic bytes per launch / average launch time vs the measured HBM copy bandwidth
+  cpu_baseline the C restatement of the reference's sequential scan on this host's cores, on a bounded
+              sample of the same workload (rank 0, N = 1 only)
+--impl reference times that CPU scan alone (the reference itself is Python + Metal through MLX and has
+no CPU-runnable build here), on the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "scan Gelem/s + % HBM peak at L=4k; Mamba-2.8b decode tok/s at 1/2/4/8 GPU"
+CFG = dict(batch=8, dim=1536, dstate=16, seqlen=4096)
+
+
+def scan_bytes(batch, dim, dstate, seqlen, s_io=2, s_bc=2):
+    """Algorithmic HBM bytes of one configs[1] launch: u, delta, z read + y written (s_io each per
+    (b,d,t)), B and C read once (s_bc per (b,n,t)), A and D read, the fp32 final state written."""
+    return (4 * s_io * batch * dim * seqlen + 2 * s_bc * batch * dstate * seqlen + 4 * dim * dstate + 4 * dim
+            + 4 * batch * dim * dstate)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the scan kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "scan_config1_traffic.json"
+    if p.exists():
+        return json.loads(p.read_text()).get("dram_bytes_per_launch")
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the timed region runs."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return None
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 7:
+                try:
+                    rows.append((float(parts[0]), float(parts[1]), parts[3:7]))
+                except ValueError:
+                    pass
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def make_inputs(seed=0):
+    from oracle.scan_ref import make_baseline_inputs
+
+    return make_baseline_inputs(CFG["batch"], CFG["dim"], CFG["dstate"], CFG["seqlen"], seed=seed)
+
+
+def cpu_scan_rate(inp, budget_s=10.0):
+    """Times the C oracle (sequential scan, OpenMP over (batch, channel), all host threads) on a
+    bounded sample of the configs[1] batch: whole (batch, channel) rows, as many as fit the time budget
+    (the full batch when it does); returns (Gelem/s, threads, sample description)."""
+    from oracle.scan_c import max_threads, selective_scan_c
+
+    threads = max_threads()
+    nb, dim = inp["u"].shape[0], inp["u"].shape[1]
+
+    def run(rows):
+        b = (rows + dim - 1) // dim
+        c = rows if b == 1 else dim
+        sl = lambda a: np.ascontiguousarray(a[:b, :c])
+        t0 = time.perf_counter()
+        selective_scan_c(sl(inp["u"]), sl(inp["delta"]), inp["A"][:c], inp["B"][:b], inp["C"][:b], inp["D"][:c],
+                         sl(inp["z"]), delta_softplus=True, threads=threads)
+        return time.perf_counter() - t0, b, c
+
+    dt, b, c = run(max(threads, 32))
+    rows = int(min(nb * dim, max(b * c, b * c * budget_s / max(dt, 1e-3))))
+    dt, b, c = run(rows)
+    elems = b * c * CFG["seqlen"]
+    return elems / dt / 1e9, threads, (f"configs[1]: batches 0..{b - 1} x channels 0..{c - 1} x all {CFG['seqlen']} "
+                                       f"steps ({elems} elements, {dt:.1f} s), fp32 math on the fp32 inputs")
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    inp = make_inputs()
+    for _ in range(args.warmup):
+        cpu_scan_rate(inp, budget_s=1.0)
+    rates = []
+    for _ in range(args.steps):
+        r, threads, sample = cpu_scan_rate(inp, budget_s=max(2.0, 60.0 / max(args.steps, 1)))
+        rates.append(r)
+    value = statistics.median(rates)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "Gelem/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (BASELINE configs[1] "
+            "distributions, seed 0)",
+            "config": {"workload": "selective_scan configs[1] (bounded CPU sample)", **CFG, "fp16_inputs": True},
+            "cpu_baseline": {"value": value, "unit": "Gelem/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "Gelem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from mamba_metal_b200 import selective_scan
+    from mamba_metal_b200.selective_scan import selective_scan_into
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    inp = make_inputs(seed=0)
+    h16 = {k: torch.from_numpy(inp[k]).to(torch.float16).pin_memory() for k in ("u", "delta", "z", "B", "C")}
+    h32 = {k: torch.from_numpy(inp[k]).pin_memory() for k in ("A", "D")}
+    d = {k: v.to(dev, non_blocking=True) for k, v in {**h16, **h32}.items()}
+    b, dm, n, L = CFG["batch"], CFG["dim"], CFG["dstate"], CFG["seqlen"]
+    y = torch.empty((b, dm, L), dtype=torch.float16, device=dev)
+    state = torch.empty((b, dm, n), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        selective_scan_into(d["u"], d["delta"], d["A"], d["B"], d["C"], d["D"], d["z"], y, state, True)
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    sync_all()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    with ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
+                      if world == 1 else local_rank) as clk:
+        sync_all()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for k in range(args.steps):
+            ev[2 * k].record(stream)
+            step()
+            ev[2 * k + 1].record(stream)
+        t_end.record(stream)
+        sync_all()
+    total_ms = max_over_ranks(t_start.elapsed_time(t_end))
+    launch_ms = max_over_ranks(statistics.mean(ev[2 * k].elapsed_time(ev[2 * k + 1]) for k in range(args.steps)))
+    elems = b * dm * L
+    ms_per_step = total_ms / args.steps
+    value = world * elems / (ms_per_step * 1e-3) / 1e9
+
+    # e2e: public API, pinned host inputs, copies inside the timed region
+    def e2e_step():
+        dd = {k: v.to(dev, non_blocking=True) for k, v in h16.items()}
+        yy, hh = selective_scan(dd["u"], dd["delta"], d["A"], dd["B"], dd["C"], D=d["D"], z=dd["z"],
+                                delta_softplus=True, return_state=True)
+        y_host.copy_(yy, non_blocking=True)
+        s_host.copy_(hh, non_blocking=True)
+
+    y_host = torch.empty((b, dm, L), dtype=torch.float16).pin_memory()
+    s_host = torch.empty((b, dm, n), dtype=torch.float32).pin_memory()
+    for _ in range(max(1, min(args.warmup, 3))):
+        e2e_step()
+    sync_all()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    sync_all()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    h2d = sum(v.numel() * v.element_size() for v in h16.values())
+    d2h = y_host.numel() * 2 + s_host.numel() * 4
+
+    if rank != 0:
+        return
+    peak, peak_kind = load_peaks()
+    nbytes = scan_bytes(b, dm, n, L)
+    achieved = nbytes / (launch_ms * 1e-3) / 1e9
+    cpu = None
+    if world == 1:
+        rate, threads, sample = cpu_scan_rate(inp)
+        cpu = {"value": rate, "unit": "Gelem/s", "cores": threads, "kind": "port", "sample": sample}
+    line = {
+        "metric": METRIC, "value": value, "unit": "Gelem/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 in / f32 math", "data": "synthetic (BASELINE configs[1] distributions, "
+        "seed 0)",
+        "config": {"workload": "selective_scan configs[1]: fp16 u/delta/z/B/C, fp32 A/D, D skip, SiLU(z), softplus, "
+                   "final state", **CFG, "per_gpu": True, "l2": "inputs larger than L2 (400 MB per step vs 126 MB)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": load_traffic(), "peak_kind": peak_kind, "algorithmic_bytes": nbytes,
+                     "launch_ms": launch_ms},
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * elems / (e2e_ms * 1e-3) / 1e9, "unit": "Gelem/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "gpu_launches": args.steps},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,212 @@
+/*
+ * mamba_b200.h -- C-ABI of the B200 (sm_100a) selective-scan / conv1d / decode-step library.
+ *
+ * The library is libmamba_b200.so (built from mamba_metal_b200/csrc/). Every entry point takes a
+ * plain argument struct of device pointers, element strides and sizes, plus a CUDA stream handle,
+ * and returns MM_OK (0) or a negative MM_ERR_* code. No entry point aborts, allocates device memory
+ * or keeps hidden mutable state: the caller owns every buffer (outputs and workspace), and all work
+ * is ordered on the given stream. Integer fields are int64_t so the struct layout is the same for
+ * every FFI (ctypes, cgo, JNI) without padding surprises.
+ *
+ * Reference interface being replaced (createcentury/mamba-metal):
+ *   - mamba_metal/selective_scan.py:12-20 builds an mx.fast.metal_kernel over
+ *     kernels/selective_scan_chunked.metal, and selective_scan.py:62-76 calls it with
+ *     inputs=[u, delta, A, B, C, D, z, batch, dim, dstate, seqlen, apply_softplus, use_D, use_z],
+ *     output_shapes=[u.shape, (batch, dim, dstate)], output_dtypes=[u.dtype, float32].
+ *     -> mm_selective_scan_fwd (+ mm_selective_scan_workspace_size, mm_selective_scan_status).
+ *   - mamba_metal/mamba_block.py:45-52 / :129-130 (MLX nn.Conv1d, groups=d_inner, padding=d_conv-1,
+ *     output sliced to [:, :L], then nn.silu) and the conv-state capture at mamba_block.py:118-127.
+ *     -> mm_causal_conv1d_fwd.
+ *   - mamba_metal/mamba_block.py:171-177 (decode: window shift, dot with the conv weight, + bias, SiLU).
+ *     -> mm_causal_conv1d_step.
+ *   - mamba_metal/mamba_block.py:183-195 (decode: softplus(dt), h = exp(dt*A)*h + dt*x*B,
+ *     y = sum(h*C) + D*x, y *= silu(z)).
+ *     -> mm_ssm_decode_step.
+ *   - mamba_metal/mamba_model.py:49-58 and :40,:69 (pre-RMSNorm + residual around each mixer).
+ *     -> mm_add_rmsnorm.
+ */
+#ifndef MAMBA_B200_H
+#define MAMBA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t, passed opaquely so that this header does not need the CUDA headers. NULL = legacy
+ * default stream. */
+typedef void* mm_stream_t;
+
+/* Element types of activation tensors (u, delta, z, B, C, x, y). A, D, conv weights and all
+ * recurrent state are always fp32. */
+enum { MM_F32 = 0, MM_F16 = 1, MM_BF16 = 2 };
+
+enum {
+  MM_OK = 0,
+  MM_ERR_ARG = -1,       /* NULL pointer where one is required, or a negative size */
+  MM_ERR_SHAPE = -2,     /* size outside the supported range (e.g. dstate > 64, width != 4) */
+  MM_ERR_DTYPE = -3,     /* unknown dtype code */
+  MM_ERR_WORKSPACE = -4, /* workspace missing, too small or not 256-byte aligned */
+  MM_ERR_LAUNCH = -5,    /* the CUDA launch (or the workspace clear) failed */
+  MM_ERR_TIMEOUT = -6    /* a carry hand-off between warps waited past its limit (status only) */
+};
+
+/* Largest dstate the scan and the decode step accept (same limit as the reference,
+ * mamba_metal/selective_scan.py:9 MAX_DSTATE = 64). */
+#define MM_MAX_DSTATE 64
+
+/* ---------------------------------------------------------------------------------------------
+ * Selective scan forward.
+ *   delta' = softplus(delta) if delta_softplus else delta        (softplus uses the >20 cutoff)
+ *   h[t,n] = exp(delta'[t] * A[d,n]) * h[t-1,n] + delta'[t] * u[t] * B[n,t],   h[-1] = 0
+ *   y[t]   = (sum_n h[t,n] * C[n,t] + D[d] * u[t]) * silu(z[t])   (D and z optional)
+ *   state_out[b,d,n] = h[seqlen-1, n]
+ * Shapes (element strides given per tensor, any layout):
+ *   u, delta, z, y : (batch, dim, seqlen)   strides (b, d, t)
+ *   B, C           : (batch, dstate, seqlen) strides (b, n, t)
+ *   A              : (dim, dstate) fp32      strides (d, n)
+ *   D              : (dim,) fp32 contiguous, or NULL
+ *   state_out      : (batch, dim, dstate) fp32 contiguous, or NULL
+ * Replaces mamba_metal/selective_scan.py:62-76 (the mx.fast.metal_kernel call). y has dtype
+ * `dtype` (= u.dtype in the reference, selective_scan.py:73-74); the state is fp32.
+ * The workspace (size from mm_selective_scan_workspace_size, 256-byte aligned) carries the
+ * recurrent state between the warps that own consecutive pieces of one sequence; the call clears
+ * the part that must start at zero itself (one cudaMemsetAsync on `stream`). Two calls that share
+ * one workspace must not overlap in time on the GPU.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct MMScanArgs {
+  const void* u;
+  const void* delta;
+  const float* A;
+  const void* B;
+  const void* C;
+  const float* D;   /* may be NULL */
+  const void* z;    /* may be NULL */
+  void* y;
+  float* state_out; /* may be NULL */
+  int64_t dtype;
+  int64_t batch, dim, dstate, seqlen;
+  int64_t u_stride[3];
+  int64_t delta_stride[3];
+  int64_t z_stride[3];
+  int64_t y_stride[3];
+  int64_t B_stride[3];
+  int64_t C_stride[3];
+  int64_t A_stride[2];
+  int64_t delta_softplus; /* 0 / 1 */
+  int64_t piece_tiles;    /* timestep tiles per warp; 0 = chosen by the library */
+} MMScanArgs;
+
+int mm_selective_scan_workspace_size(const MMScanArgs* args, size_t* bytes);
+int mm_selective_scan_fwd(const MMScanArgs* args, void* workspace, size_t workspace_bytes,
+                          mm_stream_t stream);
+/* Synchronises `stream` and reports MM_OK or MM_ERR_TIMEOUT for the last scan that used
+ * `workspace`. Diagnostics only; the scan itself never blocks the host. */
+int mm_selective_scan_status(const void* workspace, mm_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Causal depthwise conv1d (prefill):
+ *   out[b,d,t] = act(bias[d] + sum_{k<width} weight[d,k] * x[b,d,t-width+1+k]),  x[.,.,<0] = 0
+ *   act = SiLU if silu else identity.
+ * x, out: (batch, dim, seqlen) with element strides (b, d, t) -- channel-first (t contiguous) and
+ * channels-last (d contiguous) both run on vectorised paths. weight: (dim, width) fp32 contiguous
+ * (the PyTorch / HF (dim, 1, width) layout), bias: (dim,) fp32 or NULL.
+ * conv_state (optional, fp32 (batch, dim, width) contiguous) receives the last `width` pre-conv
+ * inputs x[b,d,seqlen-width .. seqlen-1], zero-filled on the left when seqlen < width: the
+ * prefill -> decode hand-off of mamba_metal/mamba_block.py:118-127.
+ * Replaces MLX nn.Conv1d at mamba_metal/mamba_block.py:45-52, :129-130. width must be 4.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct MMConvArgs {
+  const void* x;
+  const float* weight;
+  const float* bias; /* may be NULL */
+  void* out;
+  float* conv_state; /* may be NULL */
+  int64_t dtype;
+  int64_t batch, dim, seqlen, width;
+  int64_t x_stride[3];
+  int64_t out_stride[3];
+  int64_t silu; /* 0 / 1 */
+} MMConvArgs;
+
+int mm_causal_conv1d_fwd(const MMConvArgs* args, mm_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Conv decode step (one token), in place on conv_state:
+ *   conv_state[b,d,:] <- [conv_state[b,d,1:], x[b,d]]
+ *   out[b,d] = act(bias[d] + sum_k weight[d,k] * conv_state[b,d,k])
+ * x, out: (batch, dim) with row strides; conv_state: fp32 (batch, dim, width) contiguous.
+ * Replaces mamba_metal/mamba_block.py:171-177.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct MMConvStepArgs {
+  const void* x;
+  float* conv_state;
+  const float* weight;
+  const float* bias; /* may be NULL */
+  void* out;
+  int64_t dtype;
+  int64_t batch, dim, width;
+  int64_t x_stride_b, out_stride_b;
+  int64_t silu;
+} MMConvStepArgs;
+
+int mm_causal_conv1d_step(const MMConvStepArgs* args, mm_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * SSM decode step (one token), in place on ssm_state:
+ *   dt' = softplus(dt) if dt_softplus else dt
+ *   h[b,d,n] <- exp(dt'*A[d,n]) * h[b,d,n] + dt' * x[b,d] * B[b,n]
+ *   y[b,d]   = (sum_n h[b,d,n] * C[b,n] + D[d] * x[b,d]) * silu(z[b,d])      (D, z optional)
+ * x, dt, z, y: (batch, dim) with row strides; B, C: (batch, dstate) with row strides (the
+ * x_proj output slices); A: (dim, dstate) fp32 contiguous; ssm_state: fp32 (batch, dim, dstate)
+ * contiguous. Replaces mamba_metal/mamba_block.py:183-195.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct MMSSMStepArgs {
+  const void* x;
+  const void* dt;
+  const void* z; /* may be NULL */
+  const void* B;
+  const void* C;
+  const float* A;
+  const float* D; /* may be NULL */
+  float* ssm_state;
+  void* y;
+  int64_t dtype;
+  int64_t batch, dim, dstate;
+  int64_t x_stride_b, dt_stride_b, z_stride_b, B_stride_b, C_stride_b, y_stride_b;
+  int64_t dt_softplus; /* 0 / 1 */
+} MMSSMStepArgs;
+
+int mm_ssm_decode_step(const MMSSMStepArgs* args, mm_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Residual add + RMSNorm over the last dimension (rows of length `dim`):
+ *   if delta != NULL: residual[r,:] += delta[r,:]          (residual is fp32, updated in place)
+ *   out[r,:] = residual[r,:] * rsqrt(mean(residual[r,:]^2) + eps) * weight[:]
+ * residual: fp32 (rows, dim) contiguous; delta, out: dtype `dtype`, rows contiguous with row
+ * strides; weight: fp32 (dim,). Replaces the pre-norm residual wrapper of
+ * mamba_metal/mamba_model.py:49-58 (nn.RMSNorm at :40, eps at :32) and norm_f at :69, :76.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct MMAddNormArgs {
+  float* residual;
+  const void* delta; /* may be NULL */
+  const float* weight;
+  void* out;
+  int64_t dtype;
+  int64_t rows, dim;
+  int64_t delta_stride_r, out_stride_r;
+  double eps;
+} MMAddNormArgs;
+
+int mm_add_rmsnorm(const MMAddNormArgs* args, mm_stream_t stream);
+
+/* Library version string (static storage). */
+const char* mm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBA_B200_H */

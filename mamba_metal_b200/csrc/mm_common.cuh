@@ -1,0 +1,155 @@
+// Shared device helpers for the sm_100a kernels of libmamba_b200.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mamba_b200.h"
+
+#define MM_DEV __device__ __forceinline__
+
+namespace mm {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ---- MUFU approximations (hardware ex2/lg2/rcp; relative error ~2^-22) ------------------------
+MM_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+MM_DEV float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+MM_DEV float rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ---- Packed fp32 pairs (Blackwell f32x2 ALU ops: one issue slot for two lanes of math) ---------
+typedef unsigned long long f2_t;
+
+MM_DEV f2_t f2_pack(float lo, float hi) {
+  f2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+MM_DEV float2 f2_unpack(f2_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+MM_DEV f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
+  f2_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+MM_DEV f2_t f2_mul(f2_t a, f2_t b) {
+  f2_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// ---- Softplus in the log2 domain --------------------------------------------------------------
+// Returns softplus(x) * log2(e) = log2(1 + 2^(x*log2e)), with the reference's cutoff
+// (mamba_metal/kernels/selective_scan_chunked.metal:60-65: x > 20 -> x). log1p is evaluated with
+// the u = 1 + e, log(u) * e / (u - 1) identity so small softplus values keep full relative accuracy.
+MM_DEV float softplus_log2(float x) {
+  const float y = x * kLog2e;
+  const float e = ex2(y);
+  const float u = 1.0f + e;
+  const float d = u - 1.0f;
+  const float l = lg2(u);
+  float r = (d == 0.0f) ? e * kLog2e : l * (e * rcp(d));
+  return (x <= 20.0f) ? r : y;
+}
+
+// SiLU(z) = z / (1 + exp(-z)) (reference formula, selective_scan_chunked.metal:141-144).
+MM_DEV float silu(float z) { return z * rcp(1.0f + ex2(-z * kLog2e)); }
+
+// ---- Element types ------------------------------------------------------------------------------
+template <typename T> struct ElemTraits;
+template <> struct ElemTraits<float> {
+  MM_DEV static float to_f32(float v) { return v; }
+  MM_DEV static float from_f32(float v) { return v; }
+};
+template <> struct ElemTraits<__half> {
+  MM_DEV static float to_f32(__half v) { return __half2float(v); }
+  MM_DEV static __half from_f32(float v) { return __float2half_rn(v); }
+};
+template <> struct ElemTraits<__nv_bfloat16> {
+  MM_DEV static float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+  MM_DEV static __nv_bfloat16 from_f32(float v) { return __float2bfloat16_rn(v); }
+};
+
+template <typename T> MM_DEV float ld_f32(const T* p) { return ElemTraits<T>::to_f32(*p); }
+template <typename T> MM_DEV void st_f32(T* p, float v) { *p = ElemTraits<T>::from_f32(v); }
+
+// Element k of a 16-byte register block holding 16/sizeof(T) values of T. k must be a compile-time
+// constant after unrolling; the block is never addressed through memory, so it stays in registers.
+MM_DEV unsigned u4_word(const uint4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+MM_DEV void u4_set_word(uint4& v, int i, unsigned w) {
+  if (i == 0) v.x = w;
+  else if (i == 1) v.y = w;
+  else if (i == 2) v.z = w;
+  else v.w = w;
+}
+template <typename T> MM_DEV float vec_elem(const uint4& v, int k);
+template <> MM_DEV float vec_elem<float>(const uint4& v, int k) { return __uint_as_float(u4_word(v, k)); }
+template <> MM_DEV float vec_elem<__half>(const uint4& v, int k) {
+  const unsigned w = u4_word(v, k >> 1);
+  return __half2float(__ushort_as_half((unsigned short)((k & 1) ? (w >> 16) : (w & 0xffffu))));
+}
+template <> MM_DEV float vec_elem<__nv_bfloat16>(const uint4& v, int k) {
+  const unsigned w = u4_word(v, k >> 1);
+  return __uint_as_float((k & 1) ? (w & 0xffff0000u) : (w << 16));
+}
+template <typename T> MM_DEV void vec_set(uint4& v, int k, float x);
+template <> MM_DEV void vec_set<float>(uint4& v, int k, float x) { u4_set_word(v, k, __float_as_uint(x)); }
+template <> MM_DEV void vec_set<__half>(uint4& v, int k, float x) {
+  const unsigned h = __half_as_ushort(__float2half_rn(x));
+  const unsigned w = u4_word(v, k >> 1);
+  u4_set_word(v, k >> 1, (k & 1) ? ((w & 0xffffu) | (h << 16)) : ((w & 0xffff0000u) | h));
+}
+template <> MM_DEV void vec_set<__nv_bfloat16>(uint4& v, int k, float x) {
+  const unsigned h = __bfloat16_as_ushort(__float2bfloat16_rn(x));
+  const unsigned w = u4_word(v, k >> 1);
+  u4_set_word(v, k >> 1, (k & 1) ? ((w & 0xffffu) | (h << 16)) : ((w & 0xffff0000u) | h));
+}
+
+// ---- cp.async (LDGSTS) staging --------------------------------------------------------------------
+MM_DEV unsigned smem_u32(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
+MM_DEV void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+MM_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> MM_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// ---- Memory-model helpers for carry hand-off ----------------------------------------------------
+MM_DEV unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+MM_DEV void st_release(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+MM_DEV unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+inline int dtype_size(int64_t dtype) {
+  return dtype == MM_F32 ? 4 : (dtype == MM_F16 || dtype == MM_BF16) ? 2 : 0;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace mm

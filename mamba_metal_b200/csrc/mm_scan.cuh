@@ -1,0 +1,529 @@
+// Selective-scan forward for sm_100a.
+//
+// Semantics follow mamba-metal's chunked Metal kernel (mamba_metal/kernels/selective_scan_chunked.metal):
+// softplus with the >20 cutoff (:57-65), a = exp(delta*A) and b = delta*u*B per state (:73-79), the
+// first-order recurrence h = a*h + b carried across the whole sequence (:81-137), y = D*u + sum_n h*C
+// (:49, :68, :126-128), y *= silu(z) (:140-144), and the final state h[seqlen-1] (:151-155).
+//
+// Mapping (not the reference's): a warp owns 32 channels of one batch row (lane = channel) and walks
+// time sequentially with all dstate states of its channel in registers, so each (t, state) costs one
+// exp (or one multiply when A has the S4D-real structure A[d,n] = (n+1)*A[d,0]) and three packed-f32x2
+// ops -- no per-element scan shuffles or barriers. B/C, which every channel of a batch row shares, are
+// staged per warp in shared memory ([t][n], fp32, pre-scaled) and read as warp-wide broadcasts.
+//
+// Parallelism across time: the flattened (channel group, time tile) space is cut into equal contiguous
+// ranges, one per warp. A warp whose piece starts mid-sequence first runs it from h = 0 (pass 1) and
+// publishes the piece's aggregate (local end state, sum of delta); it then obtains the true incoming
+// state by a decoupled look-back over the warps that own the earlier pieces of the same rows, and
+// recomputes the head of its piece exactly. The recurrence is linear in the incoming state, so the
+// remaining error of pass 1 at step t is sum_n C_n P_n(t) h_in_n with P_n(t) = exp(A_n * sum delta);
+// the recompute continues until max_n P_n(t) <= 2^-32 for every lane (or to the end of the piece), which
+// bounds that error far below the fp32 rounding of the reference's own dot product. Warps take their
+// piece ranges from an atomic ticket, so every warp waits only on warps that started before it.
+#pragma once
+
+#include "mm_common.cuh"
+
+namespace mm {
+namespace scan {
+
+constexpr int kWarpsPerCta = 4;
+constexpr int kHeadSteps = 32;          // minimum timesteps recomputed once the carry is known
+constexpr float kDecayCutoffLog2 = -32.0f;
+constexpr unsigned long long kSpinLimitNs = 2000000000ull;  // carry wait limit: 2 s
+
+struct Params {
+  const void* u;
+  const void* delta;
+  const void* z;
+  void* y;
+  const void* Bm;
+  const void* Cm;
+  const float* A;
+  const float* D;
+  float* state_out;
+  long long us[3], ds[3], zs[3], ys[3], Bs[3], Cs[3], As[2];
+  int batch, dim, nstate, seqlen;
+  int groups_per_batch;  // ceil(dim / 32)
+  int tiles_per_row;     // ceil(seqlen / TT)
+  long long total_tiles; // batch * groups_per_batch * tiles_per_row
+  int tiles_per_warp;
+  int n_warps;
+  int head_tiles;
+  int vec_io;  // u/delta/z/y: t-contiguous rows, 16-byte aligned
+  int vec_bc;  // B/C: t-contiguous rows, 16-byte aligned
+  int has_D;
+  int has_z;
+  // workspace
+  unsigned* ticket;
+  unsigned* err;
+  unsigned* flags;
+  float* agg;  // [n_warps][NM + 1][32]
+  float* pre;  // [n_warps][NM][32]
+};
+
+// Per-warp shared-memory staging. u/delta/z and the raw B/C rows of a tile (TT timesteps = one
+// 16-byte vector per lane and row) arrive through a kStages-deep cp.async ring; the B/C rows are then
+// converted to fp32 [t][n] (B pre-multiplied by ln2 because delta is carried in the log2 domain) for
+// warp-wide broadcast reads.
+constexpr int kStages = 3;
+
+template <typename T, int NM> struct Stage {
+  static constexpr int TT = 16 / sizeof(T);       // timesteps per tile
+  static constexpr int ROWS = (2 * NM + 31) / 32; // B/C rows staged by each lane
+  static constexpr int BCF = 2 * TT * NM + 16;    // fp32 B/C tile: B at 0, C at TT*NM + 16 (bank shift)
+};
+
+template <typename T, int NM> struct WarpSmem {
+  uint4 io[kStages][3][32];
+  uint4 bcraw[kStages][Stage<T, NM>::ROWS][32];
+  float bc[Stage<T, NM>::BCF];
+};
+
+// Per-piece context of one lane.
+template <typename T> struct Lane {
+  const T* u_row;
+  const T* d_row;
+  const T* z_row;
+  T* y_row;
+  const T* B_base;  // B + b * Bs[0]
+  const T* C_base;
+  int b, d, active;
+};
+
+// Issues the copies of the tile starting at t0 into ring slot `slot` (vector path: cp.async; partial,
+// strided or unaligned tiles: plain loads and shared stores, visible after the next __syncwarp).
+template <typename T, int NM>
+MM_DEV void issue_tile(WarpSmem<T, NM>& sm, int slot, const Params& p, const Lane<T>& ln, int t0, int lane) {
+  constexpr int TT = Stage<T, NM>::TT;
+  const bool full = (t0 + TT) <= p.seqlen;
+  if (p.vec_io && full) {
+    cp_async16(&sm.io[slot][0][lane], ln.u_row + t0);
+    cp_async16(&sm.io[slot][1][lane], ln.d_row + t0);
+    if (p.has_z) cp_async16(&sm.io[slot][2][lane], ln.z_row + t0);
+  } else {
+    uint4 u, d, z;
+#pragma unroll
+    for (int k = 0; k < TT; ++k) {
+      const int t = t0 + k;
+      const bool ok = t < p.seqlen;
+      vec_set<T>(u, k, ok ? ld_f32(ln.u_row + (long long)t * p.us[2]) : 0.f);
+      vec_set<T>(d, k, ok ? ld_f32(ln.d_row + (long long)t * p.ds[2]) : 0.f);
+      if (p.has_z) vec_set<T>(z, k, ok ? ld_f32(ln.z_row + (long long)t * p.zs[2]) : 0.f);
+    }
+    sm.io[slot][0][lane] = u;
+    sm.io[slot][1][lane] = d;
+    if (p.has_z) sm.io[slot][2][lane] = z;
+  }
+  // B/C rows: row r < NM is B[state r], NM <= r < 2NM is C[state r - NM].
+#pragma unroll
+  for (int j = 0; j < Stage<T, NM>::ROWS; ++j) {
+    const int r = lane + 32 * j;
+    const bool isC = r >= NM;
+    const int n = isC ? r - NM : r;
+    if (r >= 2 * NM || n >= p.nstate) {
+      sm.bcraw[slot][j][lane] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const T* row = (isC ? ln.C_base : ln.B_base) + (long long)n * (isC ? p.Cs[1] : p.Bs[1]);
+    if (p.vec_bc && full) {
+      cp_async16(&sm.bcraw[slot][j][lane], row + t0);
+    } else {
+      const long long st = isC ? p.Cs[2] : p.Bs[2];
+      uint4 v;
+#pragma unroll
+      for (int k = 0; k < TT; ++k) {
+        const int t = t0 + k;
+        vec_set<T>(v, k, t < p.seqlen ? ld_f32(row + (long long)t * st) : 0.f);
+      }
+      sm.bcraw[slot][j][lane] = v;
+    }
+  }
+}
+
+template <typename T, int NM>
+MM_DEV void convert_bc(WarpSmem<T, NM>& sm, int slot, int lane) {
+  constexpr int TT = Stage<T, NM>::TT;
+#pragma unroll
+  for (int j = 0; j < Stage<T, NM>::ROWS; ++j) {
+    const int r = lane + 32 * j;
+    if (r < 2 * NM) {
+      const bool isC = r >= NM;
+      const int n = isC ? r - NM : r;
+      const uint4 v = sm.bcraw[slot][j][lane];
+      float* dst = sm.bc + (isC ? TT * NM + 16 : 0) + n;
+      const float scale = isC ? 1.0f : kLn2;
+#pragma unroll
+      for (int k = 0; k < TT; ++k) dst[k * NM] = vec_elem<T>(v, k) * scale;
+    }
+  }
+}
+
+// Runs the recurrence over one staged tile. WY: compute and store y. ST: A has the S4D-real structure.
+template <typename T, int NM, bool SP, bool WY, bool ST, bool FULL>
+MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
+                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
+                         const Params& p, int t0, int lane) {
+  constexpr int TT = Stage<T, NM>::TT;
+  const uint4 tu = sm.io[slot][0][lane];
+  const uint4 td = sm.io[slot][1][lane];
+  uint4 tz = make_uint4(0, 0, 0, 0);
+  if (WY && p.has_z) tz = sm.io[slot][2][lane];
+  const float* sB = sm.bc;
+  const float* sC = sm.bc + TT * NM + 16;
+  uint4 yv = make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int k = 0; k < TT; ++k) {
+    if (FULL || k < nsteps) {
+      const float x = vec_elem<T>(tu, k);
+      const float dr = vec_elem<T>(td, k);
+      const float d2 = SP ? softplus_log2(dr) : dr * kLog2e;
+      sum_d2 += d2;
+      if (!SP) min_d2 = fminf(min_d2, d2);
+      const f2_t du2 = f2_pack(d2 * x, d2 * x);
+      const float4* b4 = reinterpret_cast<const float4*>(sB + k * NM);
+      const float4* c4 = reinterpret_cast<const float4*>(sC + k * NM);
+      f2_t y2 = f2_pack(0.f, 0.f);
+      f2_t a = 0, rr = 0;
+      if (ST) {
+        const float r = ex2(d2 * A0);
+        const float r2 = r * r;
+        a = f2_pack(r, r2);
+        rr = f2_pack(r2, r2);
+      }
+      const f2_t dd2 = f2_pack(d2, d2);
+#pragma unroll
+      for (int q = 0; q < NM / 4; ++q) {
+        const float4 bq = b4[q];
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          const int pi = 2 * q + s;
+          f2_t ap;
+          if (ST) {
+            if (pi > 0) a = f2_mul(a, rr);
+            ap = a;
+          } else {
+            const float2 arg = f2_unpack(f2_mul(dd2, A2[pi]));
+            ap = f2_pack(ex2(arg.x), ex2(arg.y));
+          }
+          const f2_t bb = s == 0 ? f2_pack(bq.x, bq.y) : f2_pack(bq.z, bq.w);
+          h[pi] = f2_fma(ap, h[pi], f2_mul(du2, bb));
+        }
+        if (WY) {
+          const float4 cq = c4[q];
+          y2 = f2_fma(h[2 * q], f2_pack(cq.x, cq.y), y2);
+          y2 = f2_fma(h[2 * q + 1], f2_pack(cq.z, cq.w), y2);
+        }
+      }
+      if (WY) {
+        const float2 ys = f2_unpack(y2);
+        float yk = fmaf(Dv, x, ys.x + ys.y);
+        if (p.has_z) yk *= silu(vec_elem<T>(tz, k));
+        vec_set<T>(yv, k, yk);
+      }
+    }
+  }
+  if (WY && ln.active) {
+    if (FULL && p.vec_io) {
+      __stcs(reinterpret_cast<uint4*>(ln.y_row + t0), yv);
+    } else {
+#pragma unroll
+      for (int k = 0; k < TT; ++k)
+        if (k < nsteps) st_f32(ln.y_row + (long long)(t0 + k) * p.ys[2], vec_elem<T>(yv, k));
+    }
+  }
+}
+
+// Runs the recurrence over timesteps [t_begin, t_end) (t_begin tile-aligned), keeping kStages - 1
+// tiles of copies in flight ahead of the one being computed.
+template <typename T, int NM, bool SP, bool WY, bool ST>
+MM_DEV void run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end, f2_t (&h)[NM / 2],
+                      const f2_t (&A2)[NM / 2], float A0, float Dv, float& sum_d2, float& min_d2,
+                      WarpSmem<T, NM>& sm, int lane) {
+  constexpr int TT = Stage<T, NM>::TT;
+  if (t_begin >= t_end) return;
+  const int ntiles = (t_end - t_begin + TT - 1) / TT;
+  __syncwarp();  // earlier readers of the ring and of the B/C buffer are done
+#pragma unroll
+  for (int i = 0; i < kStages - 1; ++i) {
+    if (i < ntiles) issue_tile<T, NM>(sm, i, p, ln, t_begin + i * TT, lane);
+    cp_async_commit();
+  }
+  for (int i = 0; i < ntiles; ++i) {
+    const int nx = i + kStages - 1;
+    if (nx < ntiles) issue_tile<T, NM>(sm, nx % kStages, p, ln, t_begin + nx * TT, lane);
+    cp_async_commit();
+    cp_async_wait<kStages - 1>();
+    __syncwarp();
+    const int slot = i % kStages;
+    convert_bc<T, NM>(sm, slot, lane);
+    __syncwarp();
+    const int t0 = t_begin + i * TT;
+    const int nsteps = min(TT, t_end - t0);
+    if (nsteps == TT)
+      compute_tile<T, NM, SP, WY, ST, true>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
+    else
+      compute_tile<T, NM, SP, WY, ST, false>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
+    __syncwarp();  // B/C buffer and this slot are free for the next iteration
+  }
+  cp_async_wait<0>();
+  __syncwarp();
+}
+
+// Decoupled look-back: returns (in h_in) the true state entering the piece owned by warp `w`.
+template <int NM>
+MM_DEV void lookback(const Params& p, int w, int lane, const float (&Areg)[NM], float (&h_in)[NM]) {
+#pragma unroll
+  for (int n = 0; n < NM; ++n) h_in[n] = 0.f;
+  float qsum = 0.f;  // accumulated sum of delta2 between the predecessor's end and this piece's start
+  int pred = w - 1;
+  while (pred >= 0) {
+    unsigned f = 0;
+    if (lane == 0) {
+      const unsigned long long t_start = globaltimer_ns();
+      while ((f = ld_acquire(p.flags + pred)) == 0u) {
+        if (globaltimer_ns() - t_start > kSpinLimitNs) {
+          atomicOr(p.err, 1u);
+          f = 3u;  // give up: treat as an empty prefix
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    f = __shfl_sync(0xffffffffu, f, 0);
+    if (f == 3u) break;
+    (void)ld_acquire(p.flags + pred);  // per-lane acquire ordering for the data reads below
+    if (f == 2u) {
+      const float* src = p.pre + (long long)pred * NM * 32;
+#pragma unroll
+      for (int n = 0; n < NM; ++n) h_in[n] += ex2(Areg[n] * qsum) * __ldcg(src + n * 32 + lane);
+      break;
+    }
+    const float* src = p.agg + (long long)pred * (NM + 1) * 32;
+#pragma unroll
+    for (int n = 0; n < NM; ++n) h_in[n] += ex2(Areg[n] * qsum) * __ldcg(src + n * 32 + lane);
+    qsum += __ldcg(src + NM * 32 + lane);
+    --pred;
+  }
+}
+
+MM_DEV void publish_flag(const Params& p, int w, unsigned v, int lane) {
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) st_release(p.flags + w, v);
+}
+
+template <typename T, int NM, bool SP, bool ST>
+MM_DEV void process_piece(const Params& p, int w, int g, int tile_lo, int tile_hi, bool first_piece,
+                          WarpSmem<T, NM>& sm, int lane) {
+  constexpr int TT = Stage<T, NM>::TT;
+  Lane<T> ln;
+  ln.b = g / p.groups_per_batch;
+  const int dg = g % p.groups_per_batch;
+  ln.d = dg * 32 + lane;
+  ln.active = ln.d < p.dim;
+  const int dd = ln.active ? ln.d : p.dim - 1;
+  ln.u_row = static_cast<const T*>(p.u) + ln.b * p.us[0] + dd * p.us[1];
+  ln.d_row = static_cast<const T*>(p.delta) + ln.b * p.ds[0] + dd * p.ds[1];
+  ln.z_row = p.has_z ? static_cast<const T*>(p.z) + ln.b * p.zs[0] + dd * p.zs[1] : nullptr;
+  ln.y_row = static_cast<T*>(p.y) + ln.b * p.ys[0] + dd * p.ys[1];
+  ln.B_base = static_cast<const T*>(p.Bm) + ln.b * p.Bs[0];
+  ln.C_base = static_cast<const T*>(p.Cm) + ln.b * p.Cs[0];
+
+  // A row of this lane's channel (padding states beyond nstate: A = 0 with B = C = 0, inert).
+  const float* A_row = p.A + dd * p.As[0];
+  f2_t A2[NM / 2];
+  float A_max = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < NM / 2; ++q) {
+    const float a0 = 2 * q < p.nstate ? A_row[(2 * q) * p.As[1]] : 0.f;
+    const float a1 = 2 * q + 1 < p.nstate ? A_row[(2 * q + 1) * p.As[1]] : 0.f;
+    if (2 * q < p.nstate) A_max = fmaxf(A_max, a0);
+    if (2 * q + 1 < p.nstate) A_max = fmaxf(A_max, a1);
+    A2[q] = f2_pack(a0, a1);
+  }
+  const float A0 = A_row[0];
+  const float Dv = p.has_D ? p.D[dd] : 0.f;
+  float* so = (ln.active && p.state_out != nullptr) ? p.state_out + ((long long)ln.b * p.dim + ln.d) * p.nstate
+                                                    : nullptr;
+
+  const int t_lo = tile_lo * TT;
+  const int t_hi = min(tile_hi * TT, p.seqlen);
+  const bool from_zero = tile_lo == 0;
+  const bool to_end = tile_hi == p.tiles_per_row;
+  const int head_end = from_zero ? t_lo : min(t_lo + p.head_tiles * TT, t_hi);
+
+  f2_t h[NM / 2];
+#pragma unroll
+  for (int q = 0; q < NM / 2; ++q) h[q] = f2_pack(0.f, 0.f);
+  float acc = 0.f, min_d2 = INFINITY;
+
+  // Pass 1 over the head: state only (its y is produced by the exact recompute below).
+  run_range<T, NM, SP, false, ST>(p, ln, t_lo, head_end, h, A2, A0, Dv, acc, min_d2, sm, lane);
+
+  // Then one loop over the y-producing ranges: the rest of pass 1, and (for pieces that start
+  // mid-sequence) the recompute from the true incoming state once the look-back has produced it.
+  bool recompute = false;
+  float sum_d2 = 0.f;
+  int t = head_end, t_stop = t_hi;
+  for (;;) {
+    run_range<T, NM, SP, true, ST>(p, ln, t, t_stop, h, A2, A0, Dv, acc, min_d2, sm, lane);
+    if (!recompute) {
+      if (from_zero) {
+        if (first_piece && !to_end) {
+          float* dst = p.pre + (long long)w * NM * 32;
+#pragma unroll
+          for (int q = 0; q < NM / 2; ++q) {
+            const float2 v = f2_unpack(h[q]);
+            __stcg(dst + (2 * q) * 32 + lane, v.x);
+            __stcg(dst + (2 * q + 1) * 32 + lane, v.y);
+          }
+          publish_flag(p, w, 2u, lane);
+        }
+        break;
+      }
+      sum_d2 = acc;
+      if (first_piece && !to_end) {
+        float* dst = p.agg + (long long)w * (NM + 1) * 32;
+#pragma unroll
+        for (int q = 0; q < NM / 2; ++q) {
+          const float2 v = f2_unpack(h[q]);
+          __stcg(dst + (2 * q) * 32 + lane, v.x);
+          __stcg(dst + (2 * q + 1) * 32 + lane, v.y);
+        }
+        __stcg(dst + NM * 32 + lane, sum_d2);
+        publish_flag(p, w, 1u, lane);
+      }
+      float Areg[NM];
+#pragma unroll
+      for (int n = 0; n < NM; ++n) Areg[n] = n < p.nstate ? A_row[n * p.As[1]] : 0.f;
+      float h_in[NM];
+      lookback<NM>(p, w, lane, Areg, h_in);
+      // end state = local end state + decay over the whole piece applied to the incoming state
+      f2_t h_end[NM / 2];
+#pragma unroll
+      for (int q = 0; q < NM / 2; ++q) {
+        const float2 v = f2_unpack(h[q]);
+        h_end[q] = f2_pack(v.x + ex2(Areg[2 * q] * sum_d2) * h_in[2 * q],
+                           v.y + ex2(Areg[2 * q + 1] * sum_d2) * h_in[2 * q + 1]);
+      }
+      if (first_piece && !to_end) {
+        float* dst = p.pre + (long long)w * NM * 32;
+#pragma unroll
+        for (int q = 0; q < NM / 2; ++q) {
+          const float2 v = f2_unpack(h_end[q]);
+          __stcg(dst + (2 * q) * 32 + lane, v.x);
+          __stcg(dst + (2 * q + 1) * 32 + lane, v.y);
+        }
+        publish_flag(p, w, 2u, lane);
+      }
+      if (to_end && so) {
+        // closed-form final state; replaced below if the recompute reaches the end of the piece
+#pragma unroll
+        for (int q = 0; q < NM / 2; ++q) {
+          const float2 v = f2_unpack(h_end[q]);
+          if (2 * q < p.nstate) so[2 * q] = v.x;
+          if (2 * q + 1 < p.nstate) so[2 * q + 1] = v.y;
+        }
+      }
+      // restart from the true incoming state and recompute the head exactly
+#pragma unroll
+      for (int q = 0; q < NM / 2; ++q) h[q] = f2_pack(h_in[2 * q], h_in[2 * q + 1]);
+      recompute = true;
+      acc = 0.f;
+      t = t_lo;
+      t_stop = max(head_end, min(t_lo + TT, t_hi));
+      continue;
+    }
+    t = t_stop;
+    if (t >= t_hi) break;
+    // Continue while any lane's slowest-decaying state still carries more than 2^-32 of the incoming
+    // state; with every delta >= 0 the bound only tightens as t grows.
+    const bool decays = (A_max < 0.f) && (SP || min_d2 >= 0.f);
+    if (t >= head_end && __all_sync(0xffffffffu, decays && (A_max * acc <= kDecayCutoffLog2))) break;
+    t_stop = min(t + 4 * TT, t_hi);
+  }
+  const bool exact_end = from_zero || t >= t_hi;
+  if (to_end && so && exact_end) {
+#pragma unroll
+    for (int q = 0; q < NM / 2; ++q) {
+      const float2 v = f2_unpack(h[q]);
+      if (2 * q < p.nstate) so[2 * q] = v.x;
+      if (2 * q + 1 < p.nstate) so[2 * q + 1] = v.y;
+    }
+  }
+}
+
+template <typename T, int NM, bool SP, bool ST>
+MM_DEV void scan_warp(const Params& p, int w, WarpSmem<T, NM>& sm, int lane) {
+  const long long tpr = p.tiles_per_row;
+  const long long f0 = (long long)w * p.tiles_per_warp;
+  const long long f1 = min(f0 + p.tiles_per_warp, p.total_tiles);
+  const int g_lo = (int)(f0 / tpr);
+  const int g_hi = (int)((f1 - 1) / tpr);
+  // Highest group first: the first piece is the only one a later warp can depend on, and its
+  // aggregate is published before this warp waits on anything.
+  for (int g = g_hi; g >= g_lo; --g) {
+    const int tile_lo = (int)(max(f0, (long long)g * tpr) - (long long)g * tpr);
+    const int tile_hi = (int)(min(f1, (long long)(g + 1) * tpr) - (long long)g * tpr);
+    process_piece<T, NM, SP, ST>(p, w, g, tile_lo, tile_hi, g == g_hi, sm, lane);
+  }
+}
+
+template <typename T, int NM, bool SP>
+__global__ void __launch_bounds__(kWarpsPerCta * 32, NM <= 16 ? 4 : 2) scan_kernel(const Params p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  unsigned w = 0;
+  if (lane == 0) w = atomicAdd(p.ticket, 1u);
+  w = __shfl_sync(0xffffffffu, w, 0);
+  if ((int)w >= p.n_warps) return;
+  WarpSmem<T, NM>& sm = reinterpret_cast<WarpSmem<T, NM>*>(smem_raw)[wib];
+
+  // S4D-real structure check for the channels of this warp's pieces (A[d,n] = (n+1) A[d,0], to 4 ulp).
+  // The decision must be uniform over the warp; channels of different groups are checked piecewise.
+  const long long tpr = p.tiles_per_row;
+  const long long f0 = (long long)w * p.tiles_per_warp;
+  const long long f1 = min(f0 + p.tiles_per_warp, p.total_tiles);
+  bool st = true;
+  for (int g = (int)((f1 - 1) / tpr); g >= (int)(f0 / tpr); --g) {
+    const int d = (g % p.groups_per_batch) * 32 + lane;
+    const int dd = d < p.dim ? d : p.dim - 1;
+    const float a0 = p.A[dd * p.As[0]];
+    for (int n = 1; n < p.nstate; ++n) {
+      const float an = p.A[dd * p.As[0] + n * p.As[1]];
+      if (!(fabsf(an - (float)(n + 1) * a0) <= 4.7683716e-7f * fabsf(an))) st = false;
+    }
+  }
+  st = __all_sync(0xffffffffu, st);
+  if (st)
+    scan_warp<T, NM, SP, true>(p, (int)w, sm, lane);
+  else
+    scan_warp<T, NM, SP, false>(p, (int)w, sm, lane);
+}
+
+template <typename T, int NM, bool SP>
+cudaError_t launch_one(const Params& p, int blocks, cudaStream_t s) {
+  const size_t smem = sizeof(WarpSmem<T, NM>) * kWarpsPerCta;
+  if (smem > 48 * 1024) {  // opt-in above the default dynamic limit (idempotent, per call)
+    cudaError_t e = cudaFuncSetAttribute(scan_kernel<T, NM, SP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  scan_kernel<T, NM, SP><<<blocks, kWarpsPerCta * 32, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_typed(const Params& p, int nm, bool sp, int blocks, cudaStream_t s) {
+  if (nm == 16) return sp ? launch_one<T, 16, true>(p, blocks, s) : launch_one<T, 16, false>(p, blocks, s);
+  return sp ? launch_one<T, 64, true>(p, blocks, s) : launch_one<T, 64, false>(p, blocks, s);
+}
+
+// Defined in mm_scan_{f32,f16,bf16}.cu (one translation unit per element type, compiled in parallel).
+cudaError_t launch_f32(const Params& p, int nm, bool sp, int blocks, cudaStream_t s);
+cudaError_t launch_f16(const Params& p, int nm, bool sp, int blocks, cudaStream_t s);
+cudaError_t launch_bf16(const Params& p, int nm, bool sp, int blocks, cudaStream_t s);
+
+}  // namespace scan
+}  // namespace mm

@@ -1,0 +1,107 @@
+"""One Mamba block (mixer) on the sm_100a kernels -- drop-in for mamba_metal/mamba_block.py:27-198.
+
+Layout and semantics follow the reference block (in_proj -> causal depthwise conv + SiLU -> x_proj ->
+dt_proj -> selective scan with A = -exp(A_log), D, z gate and softplus -> out_proj), with the same
+constructor, ``__call__`` / ``prefill`` / ``step`` and HF parameter names (in_proj, conv1d, x_proj,
+dt_proj, A_log, D, out_proj). Differences, all deliberate:
+
+- Activations stay channels-last (batch, seqlen, channels) end to end: the conv and scan kernels read
+  and write strided views, so the four transposes of mamba_block.py:90-100 do not exist here.
+- ``conv1d.weight`` has PyTorch/HF's (d_inner, 1, d_conv) layout (the reference transposes HF weights
+  to MLX's (d_inner, d_conv, 1) at load_hf.py:46-50).
+- ``step`` returns new state tensors like the reference by default; ``step(..., inplace=True)``
+  updates the given conv / SSM state tensors in place (O(1) memory), which generation uses.
+- The dense projections are cuBLAS GEMMs through torch; everything else runs in libmamba_b200.so.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from mamba_metal_b200 import ops
+from mamba_metal_b200.selective_scan import selective_scan_into
+
+
+class MambaBlock(nn.Module):
+    def __init__(self, d_model: int, d_state: int = 16, d_conv: int = 4, expand: int = 2,
+                 dt_rank: int | None = None, dtype: torch.dtype = torch.float32, device=None):
+        super().__init__()
+        if d_conv != 4:
+            raise ValueError("only d_conv == 4 is implemented by the conv kernels")
+        self.d_model = d_model
+        self.d_state = d_state
+        self.d_conv = d_conv
+        self.d_inner = expand * d_model
+        self.dt_rank = math.ceil(d_model / 16) if dt_rank is None else dt_rank
+        kw = dict(dtype=dtype, device=device)
+        self.in_proj = nn.Linear(d_model, self.d_inner * 2, bias=False, **kw)
+        self.conv1d = nn.Conv1d(self.d_inner, self.d_inner, kernel_size=d_conv, groups=self.d_inner,
+                                padding=d_conv - 1, bias=True, dtype=torch.float32, device=device)
+        self.x_proj = nn.Linear(self.d_inner, self.dt_rank + 2 * d_state, bias=False, **kw)
+        self.dt_proj = nn.Linear(self.dt_rank, self.d_inner, bias=True, **kw)
+        A_init = torch.arange(1, d_state + 1, dtype=torch.float32, device=device).expand(self.d_inner, d_state)
+        self.A_log = nn.Parameter(torch.log(A_init).contiguous())
+        self.D = nn.Parameter(torch.ones(self.d_inner, dtype=torch.float32, device=device))
+        self.out_proj = nn.Linear(self.d_inner, d_model, bias=False, **kw)
+        self._A_cache = None
+
+    # A = -exp(A_log) (mamba_block.py:87, :138), cached until A_log changes
+    def _A(self) -> torch.Tensor:
+        key = (self.A_log.data_ptr(), self.A_log._version, self.A_log.device)
+        if self._A_cache is None or self._A_cache[0] != key:
+            self._A_cache = (key, (-torch.exp(self.A_log.float())).contiguous())
+        return self._A_cache[1]
+
+    def _run(self, x: torch.Tensor, want_state: bool):
+        bsz, L, _ = x.shape
+        E, N, R = self.d_inner, self.d_state, self.dt_rank
+        dt_ = self.in_proj.weight.dtype
+        xz = F.linear(x.to(dt_), self.in_proj.weight)                    # (B, L, 2E)
+        x_in = xz[..., :E].transpose(1, 2)                               # (B, E, L) view
+        z = xz[..., E:].transpose(1, 2)
+        xc = torch.empty((bsz, L, E), dtype=dt_, device=x.device)
+        conv_state = torch.empty((bsz, E, self.d_conv), dtype=torch.float32, device=x.device) if want_state else None
+        ops.causal_conv1d(x_in, self.conv1d.weight, self.conv1d.bias, silu=True, out=xc.transpose(1, 2),
+                          conv_state_out=conv_state)
+        x_dbl = F.linear(xc, self.x_proj.weight)                         # (B, L, R + 2N)
+        dt = F.linear(x_dbl[..., :R], self.dt_proj.weight, self.dt_proj.bias)  # (B, L, E), bias included
+        Bm = x_dbl[..., R:R + N].transpose(1, 2)                         # (B, N, L) view
+        Cm = x_dbl[..., R + N:].transpose(1, 2)
+        y = torch.empty((bsz, L, E), dtype=dt_, device=x.device)
+        ssm_state = torch.empty((bsz, E, N), dtype=torch.float32, device=x.device) if want_state else None
+        Df = self.D if self.D.dtype == torch.float32 else self.D.float()
+        selective_scan_into(xc.transpose(1, 2), dt.transpose(1, 2), self._A(), Bm, Cm, Df, z,
+                            y.transpose(1, 2), ssm_state, delta_softplus=True)
+        out = F.linear(y, self.out_proj.weight)
+        return out, conv_state, ssm_state
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """x: (B, L, d_model) -> (B, L, d_model) (mamba_block.py:68-102)."""
+        return self._run(x, want_state=False)[0]
+
+    def prefill(self, x: torch.Tensor):
+        """Returns (y (B, L, d_model), conv_state (B, d_inner, d_conv) fp32, ssm_state (B, d_inner,
+        d_state) fp32) -- mamba_block.py:104-153."""
+        return self._run(x, want_state=True)
+
+    def step(self, x_token: torch.Tensor, conv_state: torch.Tensor, ssm_state: torch.Tensor, inplace: bool = False):
+        """O(1) per-token forward (mamba_block.py:155-198). x_token: (B, 1, d_model).
+        Returns (y (B, 1, d_model), new_conv_state, new_ssm_state)."""
+        E, N, R = self.d_inner, self.d_state, self.dt_rank
+        dt_ = self.in_proj.weight.dtype
+        if not inplace or conv_state.dtype != torch.float32 or not conv_state.is_contiguous():
+            conv_state = conv_state.to(torch.float32, copy=True).contiguous()
+        if not inplace or ssm_state.dtype != torch.float32 or not ssm_state.is_contiguous():
+            ssm_state = ssm_state.to(torch.float32, copy=True).contiguous()
+        xz = F.linear(x_token[:, 0].to(dt_), self.in_proj.weight)       # (B, 2E)
+        xc = ops.causal_conv1d_step(xz[:, :E], conv_state, self.conv1d.weight, self.conv1d.bias, silu=True)
+        x_dbl = F.linear(xc, self.x_proj.weight)                         # (B, R + 2N)
+        dt = F.linear(x_dbl[:, :R], self.dt_proj.weight, self.dt_proj.bias)
+        Df = self.D if self.D.dtype == torch.float32 else self.D.float()
+        y = ops.ssm_decode_step(xc, dt, xz[:, E:], x_dbl[:, R:R + N], x_dbl[:, R + N:], self._A(), Df, ssm_state,
+                                dt_softplus=True)
+        return F.linear(y, self.out_proj.weight)[:, None, :], conv_state, ssm_state

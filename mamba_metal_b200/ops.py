@@ -1,0 +1,138 @@
+"""Torch-facing wrappers of the conv1d, decode-step and residual-norm kernels of libmamba_b200.so.
+
+Each function passes device pointers, strides and the current stream of the tensors' device to the
+C-ABI (include/mamba_b200.h) and raises on a non-zero status. There is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from mamba_metal_b200 import _lib
+
+D_CONV = 4
+
+
+def causal_conv1d(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *, silu: bool = True,
+                  out: torch.Tensor | None = None, conv_state_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal depthwise conv1d, width 4, as MLX nn.Conv1d(groups=dim, padding=3)[:, :L] + SiLU
+    (mamba_metal/mamba_block.py:45-52, :129-130).
+
+    x: (batch, dim, seqlen) view with any strides (channel-first and channels-last views both run on
+    vector paths); weight: (dim, 1, 4) or (dim, 4) float32; bias: (dim,) float32. ``out`` (same shape,
+    any strides) defaults to a new channel-first tensor of x.dtype. ``conv_state_out``, when given, is
+    a contiguous float32 (batch, dim, 4) tensor that receives the last 4 pre-conv inputs
+    (mamba_block.py:118-127).
+    """
+    batch, dim, seqlen = x.shape
+    w = weight.reshape(dim, -1)
+    assert w.shape[1] == D_CONV, "only d_conv == 4 is implemented"
+    dev = _lib.require_cuda(x, w, bias, out, conv_state_out)
+    if x.dtype not in _lib.DTYPE_CODE:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    w = w.float().contiguous()
+    b = None if bias is None else bias.float().contiguous()
+    if out is None:
+        out = torch.empty((batch, dim, seqlen), dtype=x.dtype, device=dev)
+    assert out.shape == x.shape and out.dtype == x.dtype
+    if conv_state_out is not None:
+        assert conv_state_out.is_contiguous() and conv_state_out.dtype == torch.float32
+        assert tuple(conv_state_out.shape) == (batch, dim, D_CONV)
+    a = _lib.MMConvArgs()
+    a.x, a.weight, a.bias, a.out, a.conv_state = x.data_ptr(), w.data_ptr(), _lib.ptr(b), out.data_ptr(), \
+        _lib.ptr(conv_state_out)
+    a.dtype = _lib.DTYPE_CODE[x.dtype]
+    a.batch, a.dim, a.seqlen, a.width = batch, dim, seqlen, D_CONV
+    a.x_stride = _lib.strides3(x)
+    a.out_stride = _lib.strides3(out)
+    a.silu = int(bool(silu))
+    with torch.cuda.device(dev):
+        rc = _lib.lib().mm_causal_conv1d_fwd(ctypes.byref(a), _lib.stream_handle(dev))
+    _lib.check(rc, "mm_causal_conv1d_fwd")
+    return out
+
+
+def causal_conv1d_step(x: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+                       *, silu: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step of the conv, updating ``conv_state`` (float32 (batch, dim, 4), contiguous) in
+    place: window shift + append, dot with the weight, + bias, SiLU (mamba_block.py:171-177).
+    x: (batch, dim) with unit inner stride (row stride free). Returns out (batch, dim) of x.dtype."""
+    batch, dim = x.shape
+    assert x.stride(1) == 1
+    assert conv_state.is_contiguous() and conv_state.dtype == torch.float32
+    assert tuple(conv_state.shape) == (batch, dim, D_CONV)
+    dev = _lib.require_cuda(x, conv_state, weight, bias, out)
+    w = weight.reshape(dim, -1)
+    w = w if (w.dtype == torch.float32 and w.is_contiguous()) else w.float().contiguous()
+    b = None if bias is None else (bias if bias.dtype == torch.float32 else bias.float())
+    if out is None:
+        out = torch.empty((batch, dim), dtype=x.dtype, device=dev)
+    a = _lib.MMConvStepArgs()
+    a.x, a.conv_state, a.weight, a.bias, a.out = x.data_ptr(), conv_state.data_ptr(), w.data_ptr(), _lib.ptr(b), \
+        out.data_ptr()
+    a.dtype = _lib.DTYPE_CODE[x.dtype]
+    a.batch, a.dim, a.width = batch, dim, D_CONV
+    a.x_stride_b, a.out_stride_b = x.stride(0), out.stride(0)
+    a.silu = int(bool(silu))
+    with torch.cuda.device(dev):
+        rc = _lib.lib().mm_causal_conv1d_step(ctypes.byref(a), _lib.stream_handle(dev))
+    _lib.check(rc, "mm_causal_conv1d_step")
+    return out
+
+
+def ssm_decode_step(x, dt, z, B, C, A, D, ssm_state, *, dt_softplus: bool = True, out=None) -> torch.Tensor:
+    """One decode step of the SSM, updating ``ssm_state`` (float32 (batch, dim, dstate), contiguous) in
+    place (mamba_block.py:183-195). x, dt, z: (batch, dim); B, C: (batch, dstate) (row strides free,
+    unit inner stride); A: (dim, dstate) float32 contiguous; D: (dim,) float32 or None."""
+    batch, dim = x.shape
+    dstate = A.shape[1]
+    for t in (x, dt, z, B, C):
+        if t is not None:
+            assert t.stride(-1) == 1 and t.dtype == x.dtype
+    assert ssm_state.is_contiguous() and ssm_state.dtype == torch.float32
+    assert A.is_contiguous() and A.dtype == torch.float32
+    dev = _lib.require_cuda(x, dt, z, B, C, A, D, ssm_state, out)
+    if out is None:
+        out = torch.empty((batch, dim), dtype=x.dtype, device=dev)
+    a = _lib.MMSSMStepArgs()
+    a.x, a.dt, a.z, a.B, a.C, a.A, a.D = (_lib.ptr(t) for t in (x, dt, z, B, C, A, D))
+    a.ssm_state, a.y = ssm_state.data_ptr(), out.data_ptr()
+    a.dtype = _lib.DTYPE_CODE[x.dtype]
+    a.batch, a.dim, a.dstate = batch, dim, dstate
+    a.x_stride_b, a.dt_stride_b = x.stride(0), dt.stride(0)
+    a.z_stride_b = z.stride(0) if z is not None else 0
+    a.B_stride_b, a.C_stride_b, a.y_stride_b = B.stride(0), C.stride(0), out.stride(0)
+    a.dt_softplus = int(bool(dt_softplus))
+    with torch.cuda.device(dev):
+        rc = _lib.lib().mm_ssm_decode_step(ctypes.byref(a), _lib.stream_handle(dev))
+    _lib.check(rc, "mm_ssm_decode_step")
+    return out
+
+
+def add_rmsnorm(residual: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, eps: float,
+                out_dtype: torch.dtype, out: torch.Tensor | None = None) -> torch.Tensor:
+    """residual (float32, contiguous (..., dim)) += delta; returns RMSNorm(residual) * weight in
+    ``out_dtype`` (mamba_model.py:49-58 with nn.RMSNorm)."""
+    dim = residual.shape[-1]
+    rows = residual.numel() // dim
+    assert residual.is_contiguous() and residual.dtype == torch.float32
+    dev = _lib.require_cuda(residual, delta, weight, out)
+    w = weight if weight.dtype == torch.float32 else weight.float()
+    if delta is not None:
+        assert delta.shape == residual.shape and delta.dtype == out_dtype and delta.stride(-1) == 1
+        d2 = delta.reshape(rows, dim)
+    if out is None:
+        out = torch.empty(residual.shape, dtype=out_dtype, device=dev)
+    a = _lib.MMAddNormArgs()
+    a.residual, a.delta, a.weight, a.out = residual.data_ptr(), _lib.ptr(delta), w.data_ptr(), out.data_ptr()
+    a.dtype = _lib.DTYPE_CODE[out_dtype]
+    a.rows, a.dim = rows, dim
+    a.delta_stride_r = d2.stride(0) if delta is not None else 0
+    a.out_stride_r = out.reshape(rows, dim).stride(0)
+    a.eps = float(eps)
+    with torch.cuda.device(dev):
+        rc = _lib.lib().mm_add_rmsnorm(ctypes.byref(a), _lib.stream_handle(dev))
+    _lib.check(rc, "mm_add_rmsnorm")
+    return out

@@ -1,0 +1,81 @@
+"""The C-ABI library loads and exports every entry point include/mamba_b200.h declares; argument
+validation that needs no GPU returns the documented status codes. CPU only (no compute calls)."""
+
+import ctypes
+
+import pytest
+
+from mamba_metal_b200 import _lib
+
+
+def test_header_declares_entry_points():
+    names = _lib.header_functions()
+    assert set(names) >= {"mm_selective_scan_workspace_size", "mm_selective_scan_fwd", "mm_selective_scan_status",
+                          "mm_causal_conv1d_fwd", "mm_causal_conv1d_step", "mm_ssm_decode_step",
+                          "mm_add_rmsnorm", "mm_version"}
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    for name in _lib.header_functions():
+        assert hasattr(lib, name), f"{name} declared in include/mamba_b200.h but not exported"
+    assert b"sm_100a" in lib.mm_version()
+
+
+def test_struct_layouts_are_padding_free():
+    # all fields are 8 bytes wide, so sizeof == 8 * field count on every FFI
+    for s, n in ((_lib.MMScanArgs, 9 + 5 + 6 * 3 + 2 + 2), (_lib.MMConvArgs, 5 + 4 + 1 + 6 + 1),
+                 (_lib.MMConvStepArgs, 5 + 1 + 3 + 2 + 1), (_lib.MMSSMStepArgs, 9 + 1 + 3 + 6 + 1),
+                 (_lib.MMAddNormArgs, 4 + 1 + 2 + 2 + 1)):
+        assert ctypes.sizeof(s) == 8 * n, s.__name__
+
+
+def _scan_args(**kw):
+    a = _lib.MMScanArgs()
+    a.dtype, a.batch, a.dim, a.dstate, a.seqlen, a.piece_tiles = 1, 2, 64, 16, 1000, 4
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_workspace_size_and_validation():
+    lib = _lib.lib()
+    n = ctypes.c_size_t(0)
+    assert lib.mm_selective_scan_workspace_size(ctypes.byref(_scan_args()), ctypes.byref(n)) == 0
+    assert n.value >= 256 and n.value % 256 == 0
+    assert lib.mm_selective_scan_workspace_size(ctypes.byref(_scan_args(dstate=65)), ctypes.byref(n)) == -2
+    assert lib.mm_selective_scan_workspace_size(ctypes.byref(_scan_args(dtype=7)), ctypes.byref(n)) == -3
+    assert lib.mm_selective_scan_workspace_size(ctypes.byref(_scan_args(seqlen=-1)), ctypes.byref(n)) == -2
+    assert lib.mm_selective_scan_workspace_size(None, ctypes.byref(n)) == -1
+    # fwd rejects missing tensors / workspace before touching the device
+    a = _scan_args()
+    assert lib.mm_selective_scan_fwd(ctypes.byref(a), None, 0, None) == -1
+
+
+def test_conv_and_step_validation():
+    lib = _lib.lib()
+    c = _lib.MMConvArgs()
+    c.dtype, c.batch, c.dim, c.seqlen, c.width = 1, 1, 8, 16, 3
+    assert lib.mm_causal_conv1d_fwd(ctypes.byref(c), None) == -2  # width must be 4
+    c.width, c.dtype = 4, 9
+    assert lib.mm_causal_conv1d_fwd(ctypes.byref(c), None) == -3
+    c.dtype = 0
+    assert lib.mm_causal_conv1d_fwd(ctypes.byref(c), None) == -1  # null pointers
+    s = _lib.MMSSMStepArgs()
+    s.dtype, s.batch, s.dim, s.dstate = 0, 1, 8, 65
+    assert lib.mm_ssm_decode_step(ctypes.byref(s), None) == -2
+    r = _lib.MMAddNormArgs()
+    r.dtype, r.rows, r.dim = 0, 1, 0
+    assert lib.mm_add_rmsnorm(ctypes.byref(r), None) == -2
+
+
+def test_cpu_tensors_fail_loudly():
+    import torch
+
+    from mamba_metal_b200 import selective_scan
+
+    u = torch.zeros(1, 2, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        selective_scan(u, u, torch.zeros(2, 4), torch.zeros(1, 4, 8), torch.zeros(1, 4, 8))
+    with pytest.raises(AssertionError):
+        selective_scan(u, torch.zeros(1, 2, 9), torch.zeros(2, 4), torch.zeros(1, 4, 8), torch.zeros(1, 4, 8))

@@ -1,0 +1,141 @@
+"""MambaBlock / MambaModel / generation on the sm_100a kernels vs the float32 reference restatement."""
+
+import types
+
+import numpy as np
+import pytest
+import torch
+
+from mamba_metal_b200 import (GraphDecoder, MambaBlock, MambaConfig, MambaModel, generate, generate_fast,
+                              generate_ids, init_weights_)
+from oracle.model_ref import RefMixer, RefModel
+from tests.helpers import assert_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32():
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = old
+
+
+def small_model(seed=0, d_model=64, n_layer=2, vocab=211, dtype=torch.float32):
+    cfg = MambaConfig(d_model=d_model, n_layer=n_layer, vocab_size=vocab, dt_rank=8)
+    return cfg, init_weights_(MambaModel(cfg, dtype=dtype, device=DEV), seed=seed)
+
+
+def block_and_ref(d_model=64, seed=0):
+    cfg, m = small_model(seed, d_model=d_model, n_layer=1)
+    blk = m.layers[0].mixer
+    sd = {k.removeprefix("layers.0.mixer."): v.detach().cpu() for k, v in m.state_dict().items()
+          if k.startswith("layers.0.mixer.")}
+    return blk, RefMixer(sd, "", blk.d_state, blk.dt_rank)
+
+
+def test_block_forward_prefill_step():
+    blk, ref = block_and_ref()
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(2, 77, 64, generator=g) * 0.5
+    y = blk(x.to(DEV))
+    assert_close(y, ref.forward(x), 1e-4, "block forward")
+    y, cs, ss = blk.prefill(x.to(DEV))
+    yr, csr, ssr = ref.prefill(x)
+    assert_close(y, yr, 1e-4, "prefill y")
+    assert_close(cs, csr, 1e-5, "conv state")
+    assert_close(ss, ssr, 1e-4, "ssm state")
+    xt = torch.randn(2, 1, 64, generator=g) * 0.5
+    yt, cs2, ss2 = blk.step(xt.to(DEV), cs, ss)
+    ytr, csr2, ssr2 = ref.step(xt, csr, ssr)
+    assert_close(yt, ytr, 1e-4, "step y")
+    assert_close(cs2, csr2, 1e-5, "step conv state")
+    assert_close(ss2, ssr2, 1e-4, "step ssm state")
+    assert not torch.equal(cs, cs2)  # functional by default: inputs untouched
+
+
+def test_block_causality():
+    """experiments/11-mamba-block/test_block.py:42-61."""
+    blk, _ = block_and_ref(seed=42)
+    g = torch.Generator().manual_seed(42)
+    x1 = torch.randn(1, 64, 64, generator=g) * 0.5
+    x2 = x1.clone()
+    x2[:, 32:] = torch.randn(1, 32, 64, generator=g) * 0.5
+    y1, y2 = blk(x1.to(DEV)).cpu(), blk(x2.to(DEV)).cpu()
+    assert (y1[:, :32] - y2[:, :32]).abs().max() < 1e-4
+    assert (y1[:, 32:] - y2[:, 32:]).abs().max() > 1e-3
+
+
+def test_model_matches_reference_and_handoff():
+    cfg, m = small_model(1, n_layer=3)
+    ref = RefModel({k: v.cpu() for k, v in m.state_dict().items()}, cfg)
+    ids = torch.randint(0, cfg.vocab_size, (2, 41), generator=torch.Generator().manual_seed(3))
+    lg = m(ids.to(DEV))
+    assert lg.shape == (2, 41, cfg.vocab_size)
+    assert_close(lg, ref.forward(ids), 1e-4, "logits")
+    lp, convs, ssms = m.prefill(ids[:, :40].to(DEV))
+    lpr, convr, ssmr = ref.prefill(ids[:, :40])
+    assert_close(lp, lpr, 1e-4, "prefill logits")
+    for i in range(cfg.n_layer):
+        assert_close(convs[i], convr[i], 1e-5, f"conv state {i}")
+        assert_close(ssms[i], ssmr[i], 1e-4, f"ssm state {i}")
+    st, _, _ = m.step(ids[:, 40:41].to(DEV), convs, ssms)
+    assert_close(st[:, 0], lg[:, 40], 1e-4, "step after prefill == full forward")
+
+
+def test_graph_decoder_matches_eager():
+    cfg, m = small_model(2)
+    ids = torch.randint(0, cfg.vocab_size, (4, 9), generator=torch.Generator().manual_seed(4)).to(DEV)
+    eager = generate_ids(m, ids, 12, use_graph=False)
+    graph = generate_ids(m, ids, 12, use_graph=True)
+    assert torch.equal(eager, graph)
+
+
+class ByteTokenizer:
+    """Minimal tokenizer for tests: bytes mod vocab, no EOS."""
+
+    eos_token_id = None
+
+    def __init__(self, vocab):
+        self.vocab = vocab
+
+    def __call__(self, text, return_tensors="np"):
+        return types.SimpleNamespace(input_ids=np.array([[b % self.vocab for b in text.encode()]], dtype=np.int64))
+
+    def decode(self, ids, skip_special_tokens=True):
+        return "".join(chr(33 + (int(i) % 90)) for i in ids)
+
+
+def test_generate_fast_equals_generate():
+    """experiments/17-incremental/test_step.py:31-41: O(L^2) and O(L) greedy outputs identical."""
+    cfg, m = small_model(5)
+    tok = ByteTokenizer(cfg.vocab_size)
+    streamed = []
+    for prompt in ("Mamba is a", "Once upon a time", "The capital of Japan is"):
+        slow = generate(m, tok, prompt, max_new_tokens=16)
+        fast = generate_fast(m, tok, prompt, max_new_tokens=16, on_token=streamed.append)
+        assert slow == fast
+    assert streamed
+
+
+def test_config2_130m_prefill_and_greedy_decode():
+    """Mamba-130m architecture, random init (seed 0), fp32, one 5,601-token prompt,
+    parallel prefill, then 50 greedy decode steps; compared with the float32 reference restatement on CPU.
+    Tokens are teacher-forced from the GPU run so that a near-tie cannot cascade; every step whose
+    reference top-2 margin exceeds 1e-3 must pick the same token, and the number of closer ties is
+    reported."""
+    cfg = MambaConfig(d_model=768, n_layer=24, vocab_size=50280, d_state=16, d_conv=4, expand=2, dt_rank=48)
+    m = init_weights_(MambaModel(cfg, device=DEV), seed=0)
+    ids = torch.randint(0, cfg.vocab_size, (1, 5601), generator=torch.Generator().manual_seed(0))
+    out = generate_ids(m, ids.to(DEV), 50, use_graph=True).cpu()
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    ref = RefModel({k: v.cpu() for k, v in m.state_dict().items()}, cfg)
+    toks, logits = ref.greedy(ids, 50, forced=out)
+    top2 = torch.topk(logits[0], 2, dim=-1).values
+    margin = top2[:, 0] - top2[:, 1]
+    decided = margin > 1e-3
+    mism = (toks[0] != out[0]) & decided
+    assert not mism.any(), f"greedy token mismatch at steps {torch.nonzero(mism).flatten().tolist()}"
+    print(f"config2: {int((~decided).sum())} near-tie steps of 50; tokens identical at decided steps")
