@@ -65,54 +65,69 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons while the timed region runs."""
+    """Samples the GPU's SM clock and throttle reasons through NVML from a background thread every
+    2 ms while the timed region runs (nvidia-smi's 100 ms loop is too coarse for millisecond regions)."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = None
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+
+    def __init__(self, device_index: int):
+        self.index = device_index
+        self.samples = []
+        self._stop = None
+        self._thread = None
+        self._nvml = None
 
     def __enter__(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
-        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
+        import threading
+
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except (FileNotFoundError, OSError):
-            self.proc = None
-        time.sleep(0.3)
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            nv = self._nvml
+            while not self._stop.is_set():
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                    self.samples.append((mhz, rs))
+                except Exception:
+                    pass
+                self._stop.wait(0.002)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        if self.proc is None or not self.path:
+        if self._nvml is None or not self.samples:
             return None
-        rows = []
-        for line in Path(self.path).read_text().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 7:
-                try:
-                    rows.append((float(parts[0]), float(parts[1]), parts[3:7]))
-                except ValueError:
-                    pass
-        os.unlink(self.path)
-        if not rows:
-            return None
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+        reasons = sorted({k for _, r in self.samples for k, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples), "source": "NVML, 2 ms interval"}
+
+
+def _nvml_index(local_rank: int) -> int:
+    """NVML index of this process's GPU (CUDA_VISIBLE_DEVICES maps CUDA ordinals to physical GPUs)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",")]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
 
 
 def make_inputs(seed=0):
@@ -206,8 +221,7 @@ def run_ours(args, rank, world, local_rank):
         step()
     sync_all()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
-    with ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
-                      if world == 1 else local_rank) as clk:
+    with ClockSampler(_nvml_index(local_rank)) as clk:
         sync_all()
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
@@ -223,6 +237,13 @@ def run_ours(args, rank, world, local_rank):
     elems = b * dm * L
     ms_per_step = total_ms / args.steps
     value = world * elems / (ms_per_step * 1e-3) / 1e9
+
+    if args.no_extras:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": world * b * dm * L / (total_ms / args.steps * 1e-3) / 1e9,
+                              "unit": "Gelem/s", "ms_per_step": total_ms / args.steps, "launch_ms": launch_ms,
+                              "n_gpus": world, "note": "--no-extras: device loop only"}), flush=True)
+        return
 
     # e2e: public API, pinned host inputs, copies inside the timed region
     def e2e_step():
@@ -281,6 +302,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true", help="device loop only: no e2e arm, no CPU baseline")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
