@@ -7,11 +7,14 @@ There is no CPU or PyTorch fallback: a missing library, a CPU tensor or a non-ze
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmamba_b200.so"
+# MAMBA_B200_LIB selects another build of the same library (e.g. a variant compiled with different
+# launch bounds); by default the in-tree build is loaded.
+LIB_PATH = Path(os.environ.get("MAMBA_B200_LIB", Path(__file__).resolve().parent / "_lib" / "libmamba_b200.so"))
 HEADER_PATH = Path(__file__).resolve().parents[1] / "include" / "mamba_b200.h"
 
 MM_F32, MM_F16, MM_BF16 = 0, 1, 2

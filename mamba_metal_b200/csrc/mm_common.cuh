@@ -57,16 +57,16 @@ MM_DEV f2_t f2_mul(f2_t a, f2_t b) {
 }
 
 // ---- Softplus in the log2 domain --------------------------------------------------------------
-// Returns softplus(x) * log2(e) = log2(1 + 2^(x*log2e)), with the reference's cutoff
-// (mamba_metal/kernels/selective_scan_chunked.metal:60-65: x > 20 -> x). log1p is evaluated with
-// the u = 1 + e, log(u) * e / (u - 1) identity so small softplus values keep full relative accuracy.
+// Returns softplus(x) * log2(e) = log2(1 + e) with e = 2^(x*log2e), and the reference's cutoff
+// (mamba_metal/kernels/selective_scan_chunked.metal:60-65: x > 20 -> x). For e < 2^-6, 1 + e would lose
+// e's low bits, so log2(1 + e) comes from the series e*log2e*(1 - e/2 + e^2/3) instead (relative error
+// below 1e-6 there); above it the MUFU lg2 of 1 + e is within ~4e-6 relative.
 MM_DEV float softplus_log2(float x) {
   const float y = x * kLog2e;
   const float e = ex2(y);
-  const float u = 1.0f + e;
-  const float d = u - 1.0f;
-  const float l = lg2(u);
-  float r = (d == 0.0f) ? e * kLog2e : l * (e * rcp(d));
+  const float l = lg2(1.0f + e);
+  const float ser = e * kLog2e * fmaf(e, fmaf(e, 0.33333334f, -0.5f), 1.0f);
+  const float r = (e < 0.015625f) ? ser : l;
   return (x <= 20.0f) ? r : y;
 }
 
@@ -91,8 +91,9 @@ template <> struct ElemTraits<__nv_bfloat16> {
 template <typename T> MM_DEV float ld_f32(const T* p) { return ElemTraits<T>::to_f32(*p); }
 template <typename T> MM_DEV void st_f32(T* p, float v) { *p = ElemTraits<T>::from_f32(v); }
 
-// Element k of a 16-byte register block holding 16/sizeof(T) values of T. k must be a compile-time
-// constant after unrolling; the block is never addressed through memory, so it stays in registers.
+// Elements of a 16-byte register block holding 16/sizeof(T) values of T, handled in pairs so that
+// 16-bit types convert with one paired instruction. Indices must be compile-time constants after
+// unrolling; the block is never addressed through memory, so it stays in registers.
 MM_DEV unsigned u4_word(const uint4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
 MM_DEV void u4_set_word(uint4& v, int i, unsigned w) {
   if (i == 0) v.x = w;
@@ -100,15 +101,35 @@ MM_DEV void u4_set_word(uint4& v, int i, unsigned w) {
   else if (i == 2) v.z = w;
   else v.w = w;
 }
-template <typename T> MM_DEV float vec_elem(const uint4& v, int k);
-template <> MM_DEV float vec_elem<float>(const uint4& v, int k) { return __uint_as_float(u4_word(v, k)); }
-template <> MM_DEV float vec_elem<__half>(const uint4& v, int k) {
-  const unsigned w = u4_word(v, k >> 1);
-  return __half2float(__ushort_as_half((unsigned short)((k & 1) ? (w >> 16) : (w & 0xffffu))));
+// pair i = elements (2i, 2i+1)
+template <typename T> MM_DEV float2 vec_pair(const uint4& v, int i);
+template <> MM_DEV float2 vec_pair<float>(const uint4& v, int i) {
+  return make_float2(__uint_as_float(u4_word(v, 2 * i)), __uint_as_float(u4_word(v, 2 * i + 1)));
 }
-template <> MM_DEV float vec_elem<__nv_bfloat16>(const uint4& v, int k) {
-  const unsigned w = u4_word(v, k >> 1);
-  return __uint_as_float((k & 1) ? (w & 0xffff0000u) : (w << 16));
+template <> MM_DEV float2 vec_pair<__half>(const uint4& v, int i) {
+  const unsigned w = u4_word(v, i);
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <> MM_DEV float2 vec_pair<__nv_bfloat16>(const uint4& v, int i) {
+  const unsigned w = u4_word(v, i);
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <typename T> MM_DEV void vec_set_pair(uint4& v, int i, float a, float b);
+template <> MM_DEV void vec_set_pair<float>(uint4& v, int i, float a, float b) {
+  u4_set_word(v, 2 * i, __float_as_uint(a));
+  u4_set_word(v, 2 * i + 1, __float_as_uint(b));
+}
+template <> MM_DEV void vec_set_pair<__half>(uint4& v, int i, float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  u4_set_word(v, i, *reinterpret_cast<const unsigned*>(&h));
+}
+template <> MM_DEV void vec_set_pair<__nv_bfloat16>(uint4& v, int i, float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  u4_set_word(v, i, *reinterpret_cast<const unsigned*>(&h));
+}
+template <typename T> MM_DEV float vec_elem(const uint4& v, int k) {
+  const float2 p = vec_pair<T>(v, k >> 1);
+  return (k & 1) ? p.y : p.x;
 }
 template <typename T> MM_DEV void vec_set(uint4& v, int k, float x);
 template <> MM_DEV void vec_set<float>(uint4& v, int k, float x) { u4_set_word(v, k, __float_as_uint(x)); }

@@ -20,15 +20,22 @@ template <> MM_DEV void load8<float>(const float* p, float (&v)[kE]) {
   const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
   const uint4 b = __ldcs(reinterpret_cast<const uint4*>(p) + 1);
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    v[k] = vec_elem<float>(a, k);
-    v[k + 4] = vec_elem<float>(b, k);
+  for (int k = 0; k < 2; ++k) {
+    const float2 pa = vec_pair<float>(a, k), pb = vec_pair<float>(b, k);
+    v[2 * k] = pa.x;
+    v[2 * k + 1] = pa.y;
+    v[2 * k + 4] = pb.x;
+    v[2 * k + 5] = pb.y;
   }
 }
 template <typename T> MM_DEV void load8_16(const T* p, float (&v)[kE]) {
   const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
 #pragma unroll
-  for (int k = 0; k < 8; ++k) v[k] = vec_elem<T>(a, k);
+  for (int k = 0; k < 4; ++k) {
+    const float2 pr = vec_pair<T>(a, k);
+    v[2 * k] = pr.x;
+    v[2 * k + 1] = pr.y;
+  }
 }
 template <> MM_DEV void load8<__half>(const __half* p, float (&v)[kE]) { load8_16<__half>(p, v); }
 template <> MM_DEV void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[kE]) { load8_16<__nv_bfloat16>(p, v); }
@@ -37,9 +44,9 @@ template <typename T> MM_DEV void store8(T* p, const float (&v)[kE]);
 template <> MM_DEV void store8<float>(float* p, const float (&v)[kE]) {
   uint4 a, b;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    vec_set<float>(a, k, v[k]);
-    vec_set<float>(b, k, v[k + 4]);
+  for (int k = 0; k < 2; ++k) {
+    vec_set_pair<float>(a, k, v[2 * k], v[2 * k + 1]);
+    vec_set_pair<float>(b, k, v[2 * k + 4], v[2 * k + 5]);
   }
   __stcs(reinterpret_cast<uint4*>(p), a);
   __stcs(reinterpret_cast<uint4*>(p) + 1, b);
@@ -47,7 +54,7 @@ template <> MM_DEV void store8<float>(float* p, const float (&v)[kE]) {
 template <typename T> MM_DEV void store8_16(T* p, const float (&v)[kE]) {
   uint4 a;
 #pragma unroll
-  for (int k = 0; k < 8; ++k) vec_set<T>(a, k, v[k]);
+  for (int k = 0; k < 4; ++k) vec_set_pair<T>(a, k, v[2 * k], v[2 * k + 1]);
   __stcs(reinterpret_cast<uint4*>(p), a);
 }
 template <> MM_DEV void store8<__half>(__half* p, const float (&v)[kE]) { store8_16<__half>(p, v); }

@@ -24,7 +24,7 @@ static int resident_warps() {
   if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int v = sms * 16;  // 16 warps (4 CTAs of 4 warps) per SM for the dstate <= 16 kernels
+  const int v = sms * MM_SCAN_MIN_BLOCKS * kWarpsPerCta;  // resident warps of the dstate <= 16 kernels
   if (dev >= 0 && dev < 64) cached[dev] = v;
   return v;
 }

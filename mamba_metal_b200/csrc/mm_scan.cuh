@@ -27,6 +27,10 @@
 namespace mm {
 namespace scan {
 
+#ifndef MM_SCAN_MIN_BLOCKS
+#define MM_SCAN_MIN_BLOCKS 4  // resident 4-warp CTAs per SM the dstate <= 16 kernels are compiled for
+#endif
+
 constexpr int kWarpsPerCta = 4;
 constexpr int kHeadSteps = 32;          // minimum timesteps recomputed once the carry is known
 constexpr float kDecayCutoffLog2 = -32.0f;
@@ -173,55 +177,65 @@ MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2],
   const float* sC = sm.bc + TT * NM + 16;
   uint4 yv = make_uint4(0, 0, 0, 0);
 #pragma unroll
-  for (int k = 0; k < TT; ++k) {
-    if (FULL || k < nsteps) {
-      const float x = vec_elem<T>(tu, k);
-      const float dr = vec_elem<T>(td, k);
-      const float d2 = SP ? softplus_log2(dr) : dr * kLog2e;
-      sum_d2 += d2;
-      if (!SP) min_d2 = fminf(min_d2, d2);
-      const f2_t du2 = f2_pack(d2 * x, d2 * x);
-      const float4* b4 = reinterpret_cast<const float4*>(sB + k * NM);
-      const float4* c4 = reinterpret_cast<const float4*>(sC + k * NM);
-      f2_t y2 = f2_pack(0.f, 0.f);
-      f2_t a = 0, rr = 0;
-      if (ST) {
-        const float r = ex2(d2 * A0);
-        const float r2 = r * r;
-        a = f2_pack(r, r2);
-        rr = f2_pack(r2, r2);
-      }
-      const f2_t dd2 = f2_pack(d2, d2);
+  for (int kp = 0; kp < TT / 2; ++kp) {
+    const float2 xs = vec_pair<T>(tu, kp);
+    const float2 drs = vec_pair<T>(td, kp);
+    float2 zs = make_float2(0.f, 0.f);
+    if (WY && p.has_z) zs = vec_pair<T>(tz, kp);
+    float yk[2] = {0.f, 0.f};
 #pragma unroll
-      for (int q = 0; q < NM / 4; ++q) {
-        const float4 bq = b4[q];
+    for (int s2 = 0; s2 < 2; ++s2) {
+      const int k = 2 * kp + s2;
+      if (FULL || k < nsteps) {
+        const float x = s2 ? xs.y : xs.x;
+        const float dr = s2 ? drs.y : drs.x;
+        const float d2 = SP ? softplus_log2(dr) : dr * kLog2e;
+        sum_d2 += d2;
+        if (!SP) min_d2 = fminf(min_d2, d2);
+        const f2_t du2 = f2_pack(d2 * x, d2 * x);
+        const float4* b4 = reinterpret_cast<const float4*>(sB + k * NM);
+        const float4* c4 = reinterpret_cast<const float4*>(sC + k * NM);
+        f2_t y2 = f2_pack(0.f, 0.f);
+        f2_t a = 0, rr = 0;
+        if (ST) {
+          const float r = ex2(d2 * A0);
+          const float r2 = r * r;
+          a = f2_pack(r, r2);
+          rr = f2_pack(r2, r2);
+        }
+        const f2_t dd2 = f2_pack(d2, d2);
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          const int pi = 2 * q + s;
-          f2_t ap;
-          if (ST) {
-            if (pi > 0) a = f2_mul(a, rr);
-            ap = a;
-          } else {
-            const float2 arg = f2_unpack(f2_mul(dd2, A2[pi]));
-            ap = f2_pack(ex2(arg.x), ex2(arg.y));
+        for (int q = 0; q < NM / 4; ++q) {
+          const float4 bq = b4[q];
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            const int pi = 2 * q + s;
+            f2_t ap;
+            if (ST) {
+              if (pi > 0) a = f2_mul(a, rr);
+              ap = a;
+            } else {
+              const float2 arg = f2_unpack(f2_mul(dd2, A2[pi]));
+              ap = f2_pack(ex2(arg.x), ex2(arg.y));
+            }
+            const f2_t bb = s == 0 ? f2_pack(bq.x, bq.y) : f2_pack(bq.z, bq.w);
+            h[pi] = f2_fma(ap, h[pi], f2_mul(du2, bb));
           }
-          const f2_t bb = s == 0 ? f2_pack(bq.x, bq.y) : f2_pack(bq.z, bq.w);
-          h[pi] = f2_fma(ap, h[pi], f2_mul(du2, bb));
+          if (WY) {
+            const float4 cq = c4[q];
+            y2 = f2_fma(h[2 * q], f2_pack(cq.x, cq.y), y2);
+            y2 = f2_fma(h[2 * q + 1], f2_pack(cq.z, cq.w), y2);
+          }
         }
         if (WY) {
-          const float4 cq = c4[q];
-          y2 = f2_fma(h[2 * q], f2_pack(cq.x, cq.y), y2);
-          y2 = f2_fma(h[2 * q + 1], f2_pack(cq.z, cq.w), y2);
+          const float2 ys = f2_unpack(y2);
+          float yv_ = fmaf(Dv, x, ys.x + ys.y);
+          if (p.has_z) yv_ *= silu(s2 ? zs.y : zs.x);
+          yk[s2] = yv_;
         }
       }
-      if (WY) {
-        const float2 ys = f2_unpack(y2);
-        float yk = fmaf(Dv, x, ys.x + ys.y);
-        if (p.has_z) yk *= silu(vec_elem<T>(tz, k));
-        vec_set<T>(yv, k, yk);
-      }
     }
+    if (WY) vec_set_pair<T>(yv, kp, yk[0], yk[1]);
   }
   if (WY && ln.active) {
     if (FULL && p.vec_io) {
@@ -471,7 +485,7 @@ MM_DEV void scan_warp(const Params& p, int w, WarpSmem<T, NM>& sm, int lane) {
 }
 
 template <typename T, int NM, bool SP>
-__global__ void __launch_bounds__(kWarpsPerCta * 32, NM <= 16 ? 4 : 2) scan_kernel(const Params p) {
+__global__ void __launch_bounds__(kWarpsPerCta * 32, NM <= 16 ? MM_SCAN_MIN_BLOCKS : 2) scan_kernel(const Params p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
