@@ -105,6 +105,10 @@ int mm_selective_scan_fwd(const MMScanArgs* args, void* workspace, size_t worksp
 /* Synchronises `stream` and reports MM_OK or MM_ERR_TIMEOUT for the last scan that used
  * `workspace`. Diagnostics only; the scan itself never blocks the host. */
 int mm_selective_scan_status(const void* workspace, mm_stream_t stream);
+/* Synchronises `stream` and copies four counters of the last scan that used `workspace` into
+ * out4: carry-wait spin iterations, look-back hops, timesteps recomputed after the carry arrived,
+ * and pieces processed. Diagnostics only. */
+int mm_selective_scan_stats(const void* workspace, unsigned long long* out4, mm_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Causal depthwise conv1d (prefill):

@@ -75,6 +75,7 @@ _SIGNATURES = {
     "mm_selective_scan_workspace_size": ([ctypes.POINTER(MMScanArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "mm_selective_scan_fwd": ([ctypes.POINTER(MMScanArgs), _p, ctypes.c_size_t, _p], ctypes.c_int),
     "mm_selective_scan_status": ([_p, _p], ctypes.c_int),
+    "mm_selective_scan_stats": ([_p, ctypes.POINTER(ctypes.c_ulonglong), _p], ctypes.c_int),
     "mm_causal_conv1d_fwd": ([ctypes.POINTER(MMConvArgs), _p], ctypes.c_int),
     "mm_causal_conv1d_step": ([ctypes.POINTER(MMConvStepArgs), _p], ctypes.c_int),
     "mm_ssm_decode_step": ([ctypes.POINTER(MMSSMStepArgs), _p], ctypes.c_int),

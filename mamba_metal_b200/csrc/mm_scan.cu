@@ -56,10 +56,10 @@ static int make_plan(const MMScanArgs* a, Plan* pl) {
   tpw = std::max<long long>(1, std::min<long long>(tpw, std::max<long long>(1, pl->total_tiles)));
   pl->tiles_per_warp = (int)tpw;
   pl->n_warps = pl->total_tiles > 0 ? (int)((pl->total_tiles + tpw - 1) / tpw) : 0;
-  // workspace: [ticket, err] | flags[n_warps] | agg | pre
+  // workspace: [ticket, err, pad, stats[4]] | flags[n_warps] (one 128-byte line each) | agg | pre
   size_t off = 256;
   pl->flags_off = off;
-  off = align256(off + sizeof(unsigned) * (size_t)std::max(pl->n_warps, 1));
+  off = align256(off + sizeof(unsigned) * kFlagStride * (size_t)std::max(pl->n_warps, 1));
   pl->agg_off = off;
   off = align256(off + sizeof(float) * (size_t)pl->n_warps * (pl->NM + 1) * 32);
   pl->pre_off = off;
@@ -128,6 +128,7 @@ extern "C" int mm_selective_scan_fwd(const MMScanArgs* a, void* ws, size_t ws_by
   char* w = static_cast<char*>(ws);
   p.ticket = reinterpret_cast<unsigned*>(w);
   p.err = reinterpret_cast<unsigned*>(w) + 1;
+  p.stats = reinterpret_cast<unsigned long long*>(w + 8);
   p.flags = reinterpret_cast<unsigned*>(w + pl.flags_off);
   p.agg = reinterpret_cast<float*>(w + pl.agg_off);
   p.pre = reinterpret_cast<float*>(w + pl.pre_off);
@@ -140,6 +141,15 @@ extern "C" int mm_selective_scan_fwd(const MMScanArgs* a, void* ws, size_t ws_by
   else if (a->dtype == MM_F16) e = launch_f16(p, pl.NM, sp, blocks, s);
   else e = launch_bf16(p, pl.NM, sp, blocks, s);
   return e == cudaSuccess ? MM_OK : MM_ERR_LAUNCH;
+}
+
+extern "C" int mm_selective_scan_stats(const void* ws, unsigned long long* out4, mm_stream_t stream) {
+  if (!ws || !out4) return MM_ERR_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(out4, static_cast<const char*>(ws) + 8, 4 * sizeof(unsigned long long),
+                      cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return MM_ERR_LAUNCH;
+  return cudaStreamSynchronize(s) == cudaSuccess ? MM_OK : MM_ERR_LAUNCH;
 }
 
 extern "C" int mm_selective_scan_status(const void* ws, mm_stream_t stream) {

@@ -32,6 +32,7 @@ namespace scan {
 #endif
 
 constexpr int kWarpsPerCta = 4;
+constexpr int kFlagStride = 32;  // words between consecutive warps' flags
 constexpr int kHeadSteps = 32;          // minimum timesteps recomputed once the carry is known
 constexpr float kDecayCutoffLog2 = -32.0f;
 constexpr unsigned long long kSpinLimitNs = 2000000000ull;  // carry wait limit: 2 s
@@ -61,7 +62,8 @@ struct Params {
   // workspace
   unsigned* ticket;
   unsigned* err;
-  unsigned* flags;
+  unsigned long long* stats;  // [0] spin iterations, [1] look-back hops, [2] recomputed steps, [3] pieces
+  unsigned* flags;            // one flag per warp, kFlagStride words apart (one 128-byte line each)
   float* agg;  // [n_warps][NM + 1][32]
   float* pre;  // [n_warps][NM][32]
 };
@@ -291,22 +293,30 @@ MM_DEV void lookback(const Params& p, int w, int lane, const float (&Areg)[NM], 
   for (int n = 0; n < NM; ++n) h_in[n] = 0.f;
   float qsum = 0.f;  // accumulated sum of delta2 between the predecessor's end and this piece's start
   int pred = w - 1;
+  unsigned long long spins = 0, hops = 0;
   while (pred >= 0) {
     unsigned f = 0;
     if (lane == 0) {
-      const unsigned long long t_start = globaltimer_ns();
-      while ((f = ld_acquire(p.flags + pred)) == 0u) {
-        if (globaltimer_ns() - t_start > kSpinLimitNs) {
+      const unsigned* fp = p.flags + (long long)pred * kFlagStride;
+      unsigned ns = 32;
+      unsigned long long t_start = 0;
+      while ((f = ld_relaxed(fp)) == 0u) {
+        if (t_start == 0) t_start = globaltimer_ns();
+        else if (globaltimer_ns() - t_start > kSpinLimitNs) {
           atomicOr(p.err, 1u);
           f = 3u;  // give up: treat as an empty prefix
           break;
         }
-        __nanosleep(64);
+        __nanosleep(ns);
+        ns = min(ns * 2, 1024u);
+        ++spins;
       }
+      fence_acq_rel();  // acquire: the predecessor's data below is read after its flag
     }
     f = __shfl_sync(0xffffffffu, f, 0);
     if (f == 3u) break;
-    (void)ld_acquire(p.flags + pred);  // per-lane acquire ordering for the data reads below
+    ++hops;
+    if (lane != 0) fence_acq_rel();
     if (f == 2u) {
       const float* src = p.pre + (long long)pred * NM * 32;
 #pragma unroll
@@ -319,12 +329,16 @@ MM_DEV void lookback(const Params& p, int w, int lane, const float (&Areg)[NM], 
     qsum += __ldcg(src + NM * 32 + lane);
     --pred;
   }
+  if (lane == 0) {
+    atomicAdd(p.stats + 0, spins);
+    atomicAdd(p.stats + 1, hops);
+  }
 }
 
 MM_DEV void publish_flag(const Params& p, int w, unsigned v, int lane) {
   __threadfence();
   __syncwarp();
-  if (lane == 0) st_release(p.flags + w, v);
+  if (lane == 0) st_release(p.flags + (long long)w * kFlagStride, v);
 }
 
 template <typename T, int NM, bool SP, bool ST>
@@ -456,6 +470,10 @@ MM_DEV void process_piece(const Params& p, int w, int g, int tile_lo, int tile_h
     const bool decays = (A_max < 0.f) && (SP || min_d2 >= 0.f);
     if (t >= head_end && __all_sync(0xffffffffu, decays && (A_max * acc <= kDecayCutoffLog2))) break;
     t_stop = min(t + 4 * TT, t_hi);
+  }
+  if (lane == 0) {
+    atomicAdd(p.stats + 3, 1ull);
+    if (!from_zero) atomicAdd(p.stats + 2, (unsigned long long)(t - t_lo));
   }
   const bool exact_end = from_zero || t >= t_hi;
   if (to_end && so && exact_end) {
