@@ -22,6 +22,8 @@
 // piece ranges from an atomic ticket, so every warp waits only on warps that started before it.
 #pragma once
 
+#include <climits>
+
 #include "mm_common.cuh"
 
 namespace mm {
@@ -166,6 +168,8 @@ MM_DEV void convert_bc(WarpSmem<T, NM>& sm, int slot, int lane) {
 }
 
 // Runs the recurrence over one staged tile. WY: compute and store y. ST: A has the S4D-real structure.
+// Phase 1 computes every step's scalars (softplus(delta), exp(delta*A[0]), delta*u, D*u, SiLU(z)) --
+// independent across steps, so their MUFU latencies overlap; phase 2 is the FMA-only recurrence.
 template <typename T, int NM, bool SP, bool WY, bool ST, bool FULL>
 MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
                          float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
@@ -177,87 +181,104 @@ MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2],
   if (WY && p.has_z) tz = sm.io[slot][2][lane];
   const float* sB = sm.bc;
   const float* sC = sm.bc + TT * NM + 16;
-  uint4 yv = make_uint4(0, 0, 0, 0);
+
+  float dk[TT];   // ST: exp(delta*A[0]); general: delta * log2(e)
+  float duk[TT];  // delta * u
+  float yk[TT];   // WY: D * u, then the finished output
+  float gk[TT];   // WY: SiLU(z) (1 without z)
 #pragma unroll
   for (int kp = 0; kp < TT / 2; ++kp) {
     const float2 xs = vec_pair<T>(tu, kp);
     const float2 drs = vec_pair<T>(td, kp);
     float2 zs = make_float2(0.f, 0.f);
     if (WY && p.has_z) zs = vec_pair<T>(tz, kp);
-    float yk[2] = {0.f, 0.f};
 #pragma unroll
     for (int s2 = 0; s2 < 2; ++s2) {
       const int k = 2 * kp + s2;
-      if (FULL || k < nsteps) {
-        const float x = s2 ? xs.y : xs.x;
-        const float dr = s2 ? drs.y : drs.x;
-        const float d2 = SP ? softplus_log2(dr) : dr * kLog2e;
-        sum_d2 += d2;
-        if (!SP) min_d2 = fminf(min_d2, d2);
-        const f2_t du2 = f2_pack(d2 * x, d2 * x);
-        const float4* b4 = reinterpret_cast<const float4*>(sB + k * NM);
-        const float4* c4 = reinterpret_cast<const float4*>(sC + k * NM);
-        f2_t y2 = f2_pack(0.f, 0.f);
-        f2_t a = 0, rr = 0;
-        if (ST) {
-          const float r = ex2(d2 * A0);
-          const float r2 = r * r;
-          a = f2_pack(r, r2);
-          rr = f2_pack(r2, r2);
-        }
-        const f2_t dd2 = f2_pack(d2, d2);
-#pragma unroll
-        for (int q = 0; q < NM / 4; ++q) {
-          const float4 bq = b4[q];
-#pragma unroll
-          for (int s = 0; s < 2; ++s) {
-            const int pi = 2 * q + s;
-            f2_t ap;
-            if (ST) {
-              if (pi > 0) a = f2_mul(a, rr);
-              ap = a;
-            } else {
-              const float2 arg = f2_unpack(f2_mul(dd2, A2[pi]));
-              ap = f2_pack(ex2(arg.x), ex2(arg.y));
-            }
-            const f2_t bb = s == 0 ? f2_pack(bq.x, bq.y) : f2_pack(bq.z, bq.w);
-            h[pi] = f2_fma(ap, h[pi], f2_mul(du2, bb));
-          }
-          if (WY) {
-            const float4 cq = c4[q];
-            y2 = f2_fma(h[2 * q], f2_pack(cq.x, cq.y), y2);
-            y2 = f2_fma(h[2 * q + 1], f2_pack(cq.z, cq.w), y2);
-          }
-        }
-        if (WY) {
-          const float2 ys = f2_unpack(y2);
-          float yv_ = fmaf(Dv, x, ys.x + ys.y);
-          if (p.has_z) yv_ *= silu(s2 ? zs.y : zs.x);
-          yk[s2] = yv_;
-        }
+      const float x = s2 ? xs.y : xs.x;
+      const float dr = s2 ? drs.y : drs.x;
+      float d2 = SP ? softplus_log2(dr) : dr * kLog2e;
+      if (!FULL && k >= nsteps) d2 = 0.f;  // steps past the end: no decay, no input
+      sum_d2 += d2;
+      if (!SP) min_d2 = fminf(min_d2, d2);
+      dk[k] = ST ? ex2(d2 * A0) : d2;
+      duk[k] = d2 * x;
+      if (WY) {
+        yk[k] = Dv * x;
+        gk[k] = p.has_z ? silu(s2 ? zs.y : zs.x) : 1.0f;
       }
     }
-    if (WY) vec_set_pair<T>(yv, kp, yk[0], yk[1]);
+  }
+#pragma unroll
+  for (int k = 0; k < TT; ++k) {
+    if (FULL || k < nsteps) {
+      const f2_t du2 = f2_pack(duk[k], duk[k]);
+      const float4* b4 = reinterpret_cast<const float4*>(sB + k * NM);
+      const float4* c4 = reinterpret_cast<const float4*>(sC + k * NM);
+      f2_t y2 = f2_pack(0.f, 0.f);
+      f2_t a = 0, rr = 0, dd2 = 0;
+      if (ST) {
+        const float r = dk[k];
+        const float r2 = r * r;
+        a = f2_pack(r, r2);
+        rr = f2_pack(r2, r2);
+      } else {
+        dd2 = f2_pack(dk[k], dk[k]);
+      }
+#pragma unroll
+      for (int q = 0; q < NM / 4; ++q) {
+        const float4 bq = b4[q];
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          const int pi = 2 * q + s;
+          f2_t ap;
+          if (ST) {
+            if (pi > 0) a = f2_mul(a, rr);
+            ap = a;
+          } else {
+            const float2 arg = f2_unpack(f2_mul(dd2, A2[pi]));
+            ap = f2_pack(ex2(arg.x), ex2(arg.y));
+          }
+          const f2_t bb = s == 0 ? f2_pack(bq.x, bq.y) : f2_pack(bq.z, bq.w);
+          h[pi] = f2_fma(ap, h[pi], f2_mul(du2, bb));
+        }
+        if (WY) {
+          const float4 cq = c4[q];
+          y2 = f2_fma(h[2 * q], f2_pack(cq.x, cq.y), y2);
+          y2 = f2_fma(h[2 * q + 1], f2_pack(cq.z, cq.w), y2);
+        }
+      }
+      if (WY) {
+        const float2 ys = f2_unpack(y2);
+        yk[k] = (yk[k] + (ys.x + ys.y)) * gk[k];
+      }
+    }
   }
   if (WY && ln.active) {
     if (FULL && p.vec_io) {
+      uint4 yv;
+#pragma unroll
+      for (int kp = 0; kp < TT / 2; ++kp) vec_set_pair<T>(yv, kp, yk[2 * kp], yk[2 * kp + 1]);
       __stcs(reinterpret_cast<uint4*>(ln.y_row + t0), yv);
     } else {
 #pragma unroll
       for (int k = 0; k < TT; ++k)
-        if (k < nsteps) st_f32(ln.y_row + (long long)(t0 + k) * p.ys[2], vec_elem<T>(yv, k));
+        if (k < nsteps) st_f32(ln.y_row + (long long)(t0 + k) * p.ys[2], yk[k]);
     }
   }
 }
 
 // Runs the recurrence over timesteps [t_begin, t_end) (t_begin tile-aligned), keeping kStages - 1
-// tiles of copies in flight ahead of the one being computed.
+// tiles of copies in flight ahead of the one being computed. With `stop_from` < t_end, the loop may end
+// early at a tile boundary t >= stop_from once every lane's slowest-decaying state has decayed below
+// 2^kDecayCutoffLog2 over the range (the recompute after a carry hand-off); returns the end reached.
 template <typename T, int NM, bool SP, bool WY, bool ST>
-MM_DEV void run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end, f2_t (&h)[NM / 2],
-                      const f2_t (&A2)[NM / 2], float A0, float Dv, float& sum_d2, float& min_d2,
-                      WarpSmem<T, NM>& sm, int lane) {
+MM_DEV int run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end, f2_t (&h)[NM / 2],
+                     const f2_t (&A2)[NM / 2], float A0, float Dv, float& sum_d2, float& min_d2,
+                     WarpSmem<T, NM>& sm, int lane, int stop_from = INT_MAX, bool decays = false,
+                     float A_max = 0.f) {
   constexpr int TT = Stage<T, NM>::TT;
-  if (t_begin >= t_end) return;
+  if (t_begin >= t_end) return t_end;
   const int ntiles = (t_end - t_begin + TT - 1) / TT;
   __syncwarp();  // earlier readers of the ring and of the B/C buffer are done
 #pragma unroll
@@ -265,6 +286,7 @@ MM_DEV void run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end
     if (i < ntiles) issue_tile<T, NM>(sm, i, p, ln, t_begin + i * TT, lane);
     cp_async_commit();
   }
+  int t_done = t_end;
   for (int i = 0; i < ntiles; ++i) {
     const int nx = i + kStages - 1;
     if (nx < ntiles) issue_tile<T, NM>(sm, nx % kStages, p, ln, t_begin + nx * TT, lane);
@@ -281,9 +303,15 @@ MM_DEV void run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end
     else
       compute_tile<T, NM, SP, WY, ST, false>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
     __syncwarp();  // B/C buffer and this slot are free for the next iteration
+    if (t0 + TT >= stop_from && t0 + TT < t_end &&
+        __all_sync(0xffffffffu, decays && (A_max * sum_d2 <= kDecayCutoffLog2))) {
+      t_done = t0 + TT;
+      break;
+    }
   }
   cp_async_wait<0>();
   __syncwarp();
+  return t_done;
 }
 
 // Decoupled look-back: returns (in h_in) the true state entering the piece owned by warp `w`.
@@ -393,83 +421,83 @@ MM_DEV void process_piece(const Params& p, int w, int g, int tile_lo, int tile_h
   // mid-sequence) the recompute from the true incoming state once the look-back has produced it.
   bool recompute = false;
   float sum_d2 = 0.f;
-  int t = head_end, t_stop = t_hi;
+  int t = head_end;
+  const bool decays = A_max < 0.f;
   for (;;) {
-    run_range<T, NM, SP, true, ST>(p, ln, t, t_stop, h, A2, A0, Dv, acc, min_d2, sm, lane);
-    if (!recompute) {
-      if (from_zero) {
-        if (first_piece && !to_end) {
-          float* dst = p.pre + (long long)w * NM * 32;
-#pragma unroll
-          for (int q = 0; q < NM / 2; ++q) {
-            const float2 v = f2_unpack(h[q]);
-            __stcg(dst + (2 * q) * 32 + lane, v.x);
-            __stcg(dst + (2 * q + 1) * 32 + lane, v.y);
-          }
-          publish_flag(p, w, 2u, lane);
-        }
-        break;
-      }
-      sum_d2 = acc;
+    const int t_end_reached =
+        run_range<T, NM, SP, true, ST>(p, ln, t, t_hi, h, A2, A0, Dv, acc, min_d2, sm, lane,
+                                       recompute ? head_end : INT_MAX,
+                                       decays && (SP || min_d2 >= 0.f), A_max);
+    if (recompute) {
+      t = t_end_reached;
+      break;
+    }
+    if (from_zero) {
       if (first_piece && !to_end) {
-        float* dst = p.agg + (long long)w * (NM + 1) * 32;
+        float* dst = p.pre + (long long)w * NM * 32;
 #pragma unroll
         for (int q = 0; q < NM / 2; ++q) {
           const float2 v = f2_unpack(h[q]);
           __stcg(dst + (2 * q) * 32 + lane, v.x);
           __stcg(dst + (2 * q + 1) * 32 + lane, v.y);
         }
-        __stcg(dst + NM * 32 + lane, sum_d2);
-        publish_flag(p, w, 1u, lane);
+        publish_flag(p, w, 2u, lane);
       }
-      float Areg[NM];
-#pragma unroll
-      for (int n = 0; n < NM; ++n) Areg[n] = n < p.nstate ? A_row[n * p.As[1]] : 0.f;
-      float h_in[NM];
-      lookback<NM>(p, w, lane, Areg, h_in);
-      // end state = local end state + decay over the whole piece applied to the incoming state
-      f2_t h_end[NM / 2];
+      t = t_hi;
+      break;
+    }
+    sum_d2 = acc;
+    if (first_piece && !to_end) {
+      float* dst = p.agg + (long long)w * (NM + 1) * 32;
 #pragma unroll
       for (int q = 0; q < NM / 2; ++q) {
         const float2 v = f2_unpack(h[q]);
-        h_end[q] = f2_pack(v.x + ex2(Areg[2 * q] * sum_d2) * h_in[2 * q],
-                           v.y + ex2(Areg[2 * q + 1] * sum_d2) * h_in[2 * q + 1]);
+        __stcg(dst + (2 * q) * 32 + lane, v.x);
+        __stcg(dst + (2 * q + 1) * 32 + lane, v.y);
       }
-      if (first_piece && !to_end) {
-        float* dst = p.pre + (long long)w * NM * 32;
-#pragma unroll
-        for (int q = 0; q < NM / 2; ++q) {
-          const float2 v = f2_unpack(h_end[q]);
-          __stcg(dst + (2 * q) * 32 + lane, v.x);
-          __stcg(dst + (2 * q + 1) * 32 + lane, v.y);
-        }
-        publish_flag(p, w, 2u, lane);
-      }
-      if (to_end && so) {
-        // closed-form final state; replaced below if the recompute reaches the end of the piece
-#pragma unroll
-        for (int q = 0; q < NM / 2; ++q) {
-          const float2 v = f2_unpack(h_end[q]);
-          if (2 * q < p.nstate) so[2 * q] = v.x;
-          if (2 * q + 1 < p.nstate) so[2 * q + 1] = v.y;
-        }
-      }
-      // restart from the true incoming state and recompute the head exactly
-#pragma unroll
-      for (int q = 0; q < NM / 2; ++q) h[q] = f2_pack(h_in[2 * q], h_in[2 * q + 1]);
-      recompute = true;
-      acc = 0.f;
-      t = t_lo;
-      t_stop = max(head_end, min(t_lo + TT, t_hi));
-      continue;
+      __stcg(dst + NM * 32 + lane, sum_d2);
+      publish_flag(p, w, 1u, lane);
     }
-    t = t_stop;
-    if (t >= t_hi) break;
-    // Continue while any lane's slowest-decaying state still carries more than 2^-32 of the incoming
-    // state; with every delta >= 0 the bound only tightens as t grows.
-    const bool decays = (A_max < 0.f) && (SP || min_d2 >= 0.f);
-    if (t >= head_end && __all_sync(0xffffffffu, decays && (A_max * acc <= kDecayCutoffLog2))) break;
-    t_stop = min(t + 4 * TT, t_hi);
+    float Areg[NM];
+#pragma unroll
+    for (int n = 0; n < NM; ++n) Areg[n] = n < p.nstate ? A_row[n * p.As[1]] : 0.f;
+    float h_in[NM];
+    lookback<NM>(p, w, lane, Areg, h_in);
+    // end state = local end state + decay over the whole piece applied to the incoming state
+    f2_t h_end[NM / 2];
+#pragma unroll
+    for (int q = 0; q < NM / 2; ++q) {
+      const float2 v = f2_unpack(h[q]);
+      h_end[q] = f2_pack(v.x + ex2(Areg[2 * q] * sum_d2) * h_in[2 * q],
+                         v.y + ex2(Areg[2 * q + 1] * sum_d2) * h_in[2 * q + 1]);
+    }
+    if (first_piece && !to_end) {
+      float* dst = p.pre + (long long)w * NM * 32;
+#pragma unroll
+      for (int q = 0; q < NM / 2; ++q) {
+        const float2 v = f2_unpack(h_end[q]);
+        __stcg(dst + (2 * q) * 32 + lane, v.x);
+        __stcg(dst + (2 * q + 1) * 32 + lane, v.y);
+      }
+      publish_flag(p, w, 2u, lane);
+    }
+    if (to_end && so) {
+      // closed-form final state; replaced below if the recompute reaches the end of the piece
+#pragma unroll
+      for (int q = 0; q < NM / 2; ++q) {
+        const float2 v = f2_unpack(h_end[q]);
+        if (2 * q < p.nstate) so[2 * q] = v.x;
+        if (2 * q + 1 < p.nstate) so[2 * q + 1] = v.y;
+      }
+    }
+    // Restart from the true incoming state and recompute exactly, from the piece start until every
+    // lane's slowest state carries at most 2^kDecayCutoffLog2 of the incoming state (with every delta
+    // >= 0 the bound only tightens as t grows), but at least over the head whose y pass 1 skipped.
+#pragma unroll
+    for (int q = 0; q < NM / 2; ++q) h[q] = f2_pack(h_in[2 * q], h_in[2 * q + 1]);
+    recompute = true;
+    acc = 0.f;
+    t = t_lo;
   }
   if (lane == 0) {
     atomicAdd(p.stats + 3, 1ull);
