@@ -79,7 +79,9 @@ constexpr int kStages = 3;
 template <typename T, int NM> struct Stage {
   static constexpr int TT = 16 / sizeof(T);       // timesteps per tile
   static constexpr int ROWS = (2 * NM + 31) / 32; // B/C rows staged by each lane
-  static constexpr int BCF = 2 * TT * NM + 16;    // fp32 B/C tile: B at 0, C at TT*NM + 16 (bank shift)
+  static constexpr int PS = 2 * TT + 4;           // floats per state pair in the staged B/C tile
+  static constexpr int COFF = (NM / 2) * PS + 16; // C after B, shifted by 16 banks
+  static constexpr int BCF = COFF + (NM / 2) * PS;
 };
 
 template <typename T, int NM> struct WarpSmem {
@@ -149,9 +151,12 @@ MM_DEV void issue_tile(WarpSmem<T, NM>& sm, int slot, const Params& p, const Lan
   }
 }
 
+// Converts the staged raw B/C rows of a tile to fp32 [state pair][step][2] (B pre-multiplied by ln2
+// because delta is carried in the log2 domain), so one LDS.128 broadcast gives a state pair at two steps.
 template <typename T, int NM>
 MM_DEV void convert_bc(WarpSmem<T, NM>& sm, int slot, int lane) {
   constexpr int TT = Stage<T, NM>::TT;
+  constexpr int PS = Stage<T, NM>::PS;
 #pragma unroll
   for (int j = 0; j < Stage<T, NM>::ROWS; ++j) {
     const int r = lane + 32 * j;
@@ -159,10 +164,14 @@ MM_DEV void convert_bc(WarpSmem<T, NM>& sm, int slot, int lane) {
       const bool isC = r >= NM;
       const int n = isC ? r - NM : r;
       const uint4 v = sm.bcraw[slot][j][lane];
-      float* dst = sm.bc + (isC ? TT * NM + 16 : 0) + n;
+      float* dst = sm.bc + (isC ? Stage<T, NM>::COFF : 0) + (n >> 1) * PS + (n & 1);
       const float scale = isC ? 1.0f : kLn2;
 #pragma unroll
-      for (int k = 0; k < TT; ++k) dst[k * NM] = vec_elem<T>(v, k) * scale;
+      for (int kp = 0; kp < TT / 2; ++kp) {
+        const float2 e = vec_pair<T>(v, kp);
+        dst[(2 * kp) * 2] = e.x * scale;
+        dst[(2 * kp + 1) * 2] = e.y * scale;
+      }
     }
   }
 }
@@ -180,7 +189,7 @@ MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2],
   uint4 tz = make_uint4(0, 0, 0, 0);
   if (WY && p.has_z) tz = sm.io[slot][2][lane];
   const float* sB = sm.bc;
-  const float* sC = sm.bc + TT * NM + 16;
+  const float* sC = sm.bc + Stage<T, NM>::COFF;
 
   float dk[TT];   // ST: exp(delta*A[0]); general: delta * log2(e)
   float duk[TT];  // delta * u
@@ -209,48 +218,62 @@ MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2],
       }
     }
   }
+  // Phase 2, in sub-tiles of SK steps with the state pairs in the outer loop: for a fixed pair the h
+  // update is the only dependency from one step to the next; the decay powers, the B products and the
+  // y partial sums of the SK steps are independent of each other.
+  constexpr int SK = TT < 4 ? TT : 4;
+  constexpr int PS = Stage<T, NM>::PS;
 #pragma unroll
-  for (int k = 0; k < TT; ++k) {
-    if (FULL || k < nsteps) {
-      const f2_t du2 = f2_pack(duk[k], duk[k]);
-      const float4* b4 = reinterpret_cast<const float4*>(sB + k * NM);
-      const float4* c4 = reinterpret_cast<const float4*>(sC + k * NM);
-      f2_t y2 = f2_pack(0.f, 0.f);
-      f2_t a = 0, rr = 0, dd2 = 0;
+  for (int k0 = 0; k0 < TT; k0 += SK) {
+    f2_t a[SK], rr[SK], du2[SK], dd2[SK], y2[SK];
+#pragma unroll
+    for (int j = 0; j < SK; ++j) {
+      const int k = k0 + j;
+      du2[j] = f2_pack(duk[k], duk[k]);
+      y2[j] = f2_pack(0.f, 0.f);
       if (ST) {
         const float r = dk[k];
         const float r2 = r * r;
-        a = f2_pack(r, r2);
-        rr = f2_pack(r2, r2);
+        a[j] = f2_pack(r, r2);
+        rr[j] = f2_pack(r2, r2);
       } else {
-        dd2 = f2_pack(dk[k], dk[k]);
+        dd2[j] = f2_pack(dk[k], dk[k]);
+      }
+    }
+#pragma unroll
+    for (int pi = 0; pi < NM / 2; ++pi) {
+      float4 bq[SK / 2], cq[SK / 2];
+#pragma unroll
+      for (int j2 = 0; j2 < SK / 2; ++j2) {
+        bq[j2] = *reinterpret_cast<const float4*>(sB + pi * PS + (k0 + 2 * j2) * 2);
+        if (WY) cq[j2] = *reinterpret_cast<const float4*>(sC + pi * PS + (k0 + 2 * j2) * 2);
       }
 #pragma unroll
-      for (int q = 0; q < NM / 4; ++q) {
-        const float4 bq = b4[q];
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          const int pi = 2 * q + s;
+      for (int j = 0; j < SK; ++j) {
+        if (FULL || k0 + j < nsteps) {
+          const float4& b4 = bq[j >> 1];
+          const f2_t bb = (j & 1) ? f2_pack(b4.z, b4.w) : f2_pack(b4.x, b4.y);
           f2_t ap;
           if (ST) {
-            if (pi > 0) a = f2_mul(a, rr);
-            ap = a;
+            if (pi > 0) a[j] = f2_mul(a[j], rr[j]);
+            ap = a[j];
           } else {
-            const float2 arg = f2_unpack(f2_mul(dd2, A2[pi]));
+            const float2 arg = f2_unpack(f2_mul(dd2[j], A2[pi]));
             ap = f2_pack(ex2(arg.x), ex2(arg.y));
           }
-          const f2_t bb = s == 0 ? f2_pack(bq.x, bq.y) : f2_pack(bq.z, bq.w);
-          h[pi] = f2_fma(ap, h[pi], f2_mul(du2, bb));
-        }
-        if (WY) {
-          const float4 cq = c4[q];
-          y2 = f2_fma(h[2 * q], f2_pack(cq.x, cq.y), y2);
-          y2 = f2_fma(h[2 * q + 1], f2_pack(cq.z, cq.w), y2);
+          h[pi] = f2_fma(ap, h[pi], f2_mul(du2[j], bb));
+          if (WY) {
+            const float4& c4 = cq[j >> 1];
+            y2[j] = f2_fma(h[pi], (j & 1) ? f2_pack(c4.z, c4.w) : f2_pack(c4.x, c4.y), y2[j]);
+          }
         }
       }
-      if (WY) {
-        const float2 ys = f2_unpack(y2);
-        yk[k] = (yk[k] + (ys.x + ys.y)) * gk[k];
+    }
+    if (WY) {
+#pragma unroll
+      for (int j = 0; j < SK; ++j) {
+        const float2 ys = f2_unpack(y2[j]);
+        yk[k0 + j] = (yk[k0 + j] + (ys.x + ys.y)) * gk[k0 + j];
       }
     }
   }
