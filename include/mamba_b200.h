@@ -97,6 +97,7 @@ typedef struct MMScanArgs {
   int64_t A_stride[2];
   int64_t delta_softplus; /* 0 / 1 */
   int64_t piece_tiles;    /* timestep tiles per warp; 0 = chosen by the library */
+  int64_t options;        /* bit 0: stage tiles with cp.async / plain loads instead of TMA */
 } MMScanArgs;
 
 int mm_selective_scan_workspace_size(const MMScanArgs* args, size_t* bytes);

@@ -1,6 +1,7 @@
 // Shared device helpers for the sm_100a kernels of libmamba_b200.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -151,6 +152,43 @@ MM_DEV void cp_async16(void* smem_dst, const void* gmem_src) {
 }
 MM_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N> MM_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// ---- TMA tile loads and mbarriers (no cluster multicast anywhere) --------------------------------
+MM_DEV void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// makes barrier initialisation visible to the async proxy (TMA) before first use
+MM_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+MM_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+MM_DEV void mbar_arrive_expect_tx(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+MM_DEV bool mbar_try_wait_parity(unsigned long long* bar, unsigned parity) {
+  unsigned done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+MM_DEV unsigned long long globaltimer_ns();
+// Waits for the barrier phase with the given parity; gives up (returns false) after limit_ns.
+MM_DEV bool mbar_wait_parity_bounded(unsigned long long* bar, unsigned parity, unsigned long long limit_ns) {
+  if (mbar_try_wait_parity(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait_parity(bar, parity)) {
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+// 3-D tiled TMA load (coordinates in elements, innermost first) into shared memory, completing on bar.
+MM_DEV void tma_load_3d(void* smem_dst, const CUtensorMap* tm, int x, int y, int z, unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(smem_dst)), "l"(tm), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
 
 // ---- Memory-model helpers for carry hand-off ----------------------------------------------------
 MM_DEV unsigned ld_acquire(const unsigned* p) {

@@ -1,5 +1,7 @@
 // Host side of the selective-scan forward: work plan, workspace layout and the C-ABI entry points.
 // The device code is in mm_scan.cuh; its instantiations live in mm_scan_{f32,f16,bf16}.cu.
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 
 #include "mm_scan.cuh"
@@ -31,6 +33,42 @@ static int resident_warps() {
 
 static inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// 3-D map over a (n2, n1, n0) tensor with unit stride along n0 and element strides s1 (along n1) and s2
+// (along n2), tiled in boxes of (1, box1, box0). Fails (-> plain-load path) when TMA's rules are not met.
+static bool encode_3d(CUtensorMap* m, const void* base, int64_t dtype, long long n0, long long n1, long long n2,
+                      long long s1, long long s2, int box0, int box1) {
+  auto enc = tensor_map_encoder();
+  if (!enc || !base || !aligned16(base)) return false;
+  const int es = dtype_size(dtype);
+  if (n1 == 1) s1 = ((n0 * es + 15) / 16) * 16 / es;  // unused dimension: any legal stride
+  if (n2 == 1) s2 = s1 * n1;
+  if (s1 <= 0 || s2 <= 0 || (s1 * es) % 16 != 0 || (s2 * es) % 16 != 0) return false;
+  if ((s1 * es) >= (1LL << 40) || (s2 * es) >= (1LL << 40)) return false;
+  const CUtensorMapDataType dt = dtype == MM_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == MM_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[3] = {(cuuint64_t)n0, (cuuint64_t)n1, (cuuint64_t)n2};
+  cuuint64_t strides[2] = {(cuuint64_t)(s1 * es), (cuuint64_t)(s2 * es)};
+  cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static int make_plan(const MMScanArgs* a, Plan* pl) {
   if (!a) return MM_ERR_ARG;
   const int es = dtype_size(a->dtype);
@@ -39,7 +77,7 @@ static int make_plan(const MMScanArgs* a, Plan* pl) {
   if (a->dstate > MM_MAX_DSTATE) return MM_ERR_SHAPE;
   if (a->batch > (1 << 30) || a->dim > (1 << 30) || a->seqlen > (1 << 30)) return MM_ERR_SHAPE;
   pl->NM = a->dstate <= 16 ? 16 : 64;
-  pl->TT = 16 / es;
+  pl->TT = 32 / es;
   pl->groups_per_batch = (int)((a->dim + 31) / 32);
   pl->tiles_per_row = (int)((a->seqlen + pl->TT - 1) / pl->TT);
   pl->total_tiles = (long long)a->batch * pl->groups_per_batch * pl->tiles_per_row;
@@ -125,6 +163,18 @@ extern "C" int mm_selective_scan_fwd(const MMScanArgs* a, void* ws, size_t ws_by
   p.vec_bc = row_vec_ok(a->B, a->B_stride, es, true) && row_vec_ok(a->C, a->C_stride, es, true);
   p.has_D = a->D != nullptr;
   p.has_z = a->z != nullptr;
+  {
+    // TMA path: every tile-fed tensor t-contiguous with 16-byte aligned rows
+    const long long L = a->seqlen, nb = a->batch, nd = a->dim, nn = a->dstate;
+    bool ok = a->u_stride[2] == 1 && a->delta_stride[2] == 1 && a->B_stride[2] == 1 && a->C_stride[2] == 1 &&
+              (!a->z || a->z_stride[2] == 1);
+    ok = ok && encode_3d(&p.tm_u, a->u, a->dtype, L, nd, nb, a->u_stride[1], a->u_stride[0], pl.TT, 32);
+    ok = ok && encode_3d(&p.tm_d, a->delta, a->dtype, L, nd, nb, a->delta_stride[1], a->delta_stride[0], pl.TT, 32);
+    ok = ok && (!a->z || encode_3d(&p.tm_z, a->z, a->dtype, L, nd, nb, a->z_stride[1], a->z_stride[0], pl.TT, 32));
+    ok = ok && encode_3d(&p.tm_B, a->B, a->dtype, L, nn, nb, a->B_stride[1], a->B_stride[0], pl.TT, pl.NM);
+    ok = ok && encode_3d(&p.tm_C, a->C, a->dtype, L, nn, nb, a->C_stride[1], a->C_stride[0], pl.TT, pl.NM);
+    p.use_tma = ok && !(a->options & 1);
+  }
   char* w = static_cast<char*>(ws);
   p.ticket = reinterpret_cast<unsigned*>(w);
   p.err = reinterpret_cast<unsigned*>(w) + 1;

@@ -22,6 +22,8 @@
 // piece ranges from an atomic ticket, so every warp waits only on warps that started before it.
 #pragma once
 
+#include <cuda.h>
+
 #include <climits>
 
 #include "mm_common.cuh"
@@ -61,6 +63,8 @@ struct Params {
   int vec_bc;  // B/C: t-contiguous rows, 16-byte aligned
   int has_D;
   int has_z;
+  int use_tma;  // u/delta/z/B/C tiles arrive by TMA (tensor maps below), else by cp.async / plain loads
+  CUtensorMap tm_u, tm_d, tm_z, tm_B, tm_C;
   // workspace
   unsigned* ticket;
   unsigned* err;
@@ -70,23 +74,27 @@ struct Params {
   float* pre;  // [n_warps][NM][32]
 };
 
-// Per-warp shared-memory staging. u/delta/z and the raw B/C rows of a tile (TT timesteps = one
-// 16-byte vector per lane and row) arrive through a kStages-deep cp.async ring; the B/C rows are then
-// converted to fp32 [t][n] (B pre-multiplied by ln2 because delta is carried in the log2 domain) for
-// warp-wide broadcast reads.
-constexpr int kStages = 3;
+// Per-warp shared-memory staging. A tile is TT timesteps = 32 bytes of every row: the warp's 32 u / delta
+// / z rows (one per lane) and the 2*NM B / C rows, stored row-major ([row][32 bytes]). Tiles arrive
+// through a kStages-deep ring, by TMA (one elected lane copies [32 rows x TT] boxes, completion on an
+// mbarrier) when the tensors allow it, else by per-lane cp.async or plain loads. The B / C rows are then
+// converted to fp32 [state pair][step][2] (B pre-multiplied by ln2 because delta is carried in the log2
+// domain) for warp-wide broadcast reads.
+constexpr int kStages = 2;
 
 template <typename T, int NM> struct Stage {
-  static constexpr int TT = 16 / sizeof(T);       // timesteps per tile
-  static constexpr int ROWS = (2 * NM + 31) / 32; // B/C rows staged by each lane
+  static constexpr int TT = 32 / sizeof(T);       // timesteps per tile (two 16-byte vectors per row)
+  static constexpr int HT = TT / 2;               // timesteps per half tile (one vector)
+  static constexpr int ROWS = (2 * NM + 31) / 32; // B/C rows converted by each lane
   static constexpr int PS = 2 * TT + 4;           // floats per state pair in the staged B/C tile
   static constexpr int COFF = (NM / 2) * PS + 16; // C after B, shifted by 16 banks
   static constexpr int BCF = COFF + (NM / 2) * PS;
 };
 
-template <typename T, int NM> struct WarpSmem {
-  uint4 io[kStages][3][32];
-  uint4 bcraw[kStages][Stage<T, NM>::ROWS][32];
+template <typename T, int NM> struct __align__(128) WarpSmem {
+  uint4 io[kStages][3][32][2];       // [stage][u, delta, z][row = lane][two 16-byte vectors]
+  uint4 bcraw[kStages][2 * NM][2];   // [stage][B rows, then C rows][two vectors]
+  unsigned long long bar[kStages];   // TMA completion barriers
   float bc[Stage<T, NM>::BCF];
 };
 
@@ -98,64 +106,97 @@ template <typename T> struct Lane {
   T* y_row;
   const T* B_base;  // B + b * Bs[0]
   const T* C_base;
-  int b, d, active;
+  int b, d, dg, active;
 };
 
-// Issues the copies of the tile starting at t0 into ring slot `slot` (vector path: cp.async; partial,
-// strided or unaligned tiles: plain loads and shared stores, visible after the next __syncwarp).
+// Issues the copies of the tile starting at t0 into ring slot `slot`.
 template <typename T, int NM>
 MM_DEV void issue_tile(WarpSmem<T, NM>& sm, int slot, const Params& p, const Lane<T>& ln, int t0, int lane) {
   constexpr int TT = Stage<T, NM>::TT;
+  if (p.use_tma) {
+    if (lane == 0) {
+      // the slot was last read through the generic proxy; order those reads before the async writes
+      fence_proxy_async();
+      const unsigned bytes = (unsigned)((p.has_z ? 3 : 2) * 32 * 32 + 2 * NM * 32);
+      unsigned long long* bar = &sm.bar[slot];
+      mbar_arrive_expect_tx(bar, bytes);
+      const int d0 = ln.dg * 32;
+      tma_load_3d(&sm.io[slot][0][0][0], &p.tm_u, t0, d0, ln.b, bar);
+      tma_load_3d(&sm.io[slot][1][0][0], &p.tm_d, t0, d0, ln.b, bar);
+      if (p.has_z) tma_load_3d(&sm.io[slot][2][0][0], &p.tm_z, t0, d0, ln.b, bar);
+      tma_load_3d(&sm.bcraw[slot][0][0], &p.tm_B, t0, 0, ln.b, bar);
+      tma_load_3d(&sm.bcraw[slot][NM][0], &p.tm_C, t0, 0, ln.b, bar);
+    }
+    return;
+  }
   const bool full = (t0 + TT) <= p.seqlen;
   if (p.vec_io && full) {
-    cp_async16(&sm.io[slot][0][lane], ln.u_row + t0);
-    cp_async16(&sm.io[slot][1][lane], ln.d_row + t0);
-    if (p.has_z) cp_async16(&sm.io[slot][2][lane], ln.z_row + t0);
-  } else {
-    uint4 u, d, z;
 #pragma unroll
-    for (int k = 0; k < TT; ++k) {
-      const int t = t0 + k;
-      const bool ok = t < p.seqlen;
-      vec_set<T>(u, k, ok ? ld_f32(ln.u_row + (long long)t * p.us[2]) : 0.f);
-      vec_set<T>(d, k, ok ? ld_f32(ln.d_row + (long long)t * p.ds[2]) : 0.f);
-      if (p.has_z) vec_set<T>(z, k, ok ? ld_f32(ln.z_row + (long long)t * p.zs[2]) : 0.f);
+    for (int v = 0; v < 2; ++v) {
+      cp_async16(&sm.io[slot][0][lane][v], ln.u_row + t0 + v * (TT / 2));
+      cp_async16(&sm.io[slot][1][lane][v], ln.d_row + t0 + v * (TT / 2));
+      if (p.has_z) cp_async16(&sm.io[slot][2][lane][v], ln.z_row + t0 + v * (TT / 2));
     }
-    sm.io[slot][0][lane] = u;
-    sm.io[slot][1][lane] = d;
-    if (p.has_z) sm.io[slot][2][lane] = z;
+  } else {
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      uint4 u, d, z;
+#pragma unroll
+      for (int k = 0; k < TT / 2; ++k) {
+        const int t = t0 + v * (TT / 2) + k;
+        const bool ok = t < p.seqlen;
+        vec_set<T>(u, k, ok ? ld_f32(ln.u_row + (long long)t * p.us[2]) : 0.f);
+        vec_set<T>(d, k, ok ? ld_f32(ln.d_row + (long long)t * p.ds[2]) : 0.f);
+        if (p.has_z) vec_set<T>(z, k, ok ? ld_f32(ln.z_row + (long long)t * p.zs[2]) : 0.f);
+      }
+      sm.io[slot][0][lane][v] = u;
+      sm.io[slot][1][lane][v] = d;
+      if (p.has_z) sm.io[slot][2][lane][v] = z;
+    }
   }
   // B/C rows: row r < NM is B[state r], NM <= r < 2NM is C[state r - NM].
 #pragma unroll
   for (int j = 0; j < Stage<T, NM>::ROWS; ++j) {
     const int r = lane + 32 * j;
+    if (r >= 2 * NM) continue;
     const bool isC = r >= NM;
     const int n = isC ? r - NM : r;
-    if (r >= 2 * NM || n >= p.nstate) {
-      sm.bcraw[slot][j][lane] = make_uint4(0, 0, 0, 0);
+    if (n >= p.nstate) {
+      sm.bcraw[slot][r][0] = make_uint4(0, 0, 0, 0);
+      sm.bcraw[slot][r][1] = make_uint4(0, 0, 0, 0);
       continue;
     }
     const T* row = (isC ? ln.C_base : ln.B_base) + (long long)n * (isC ? p.Cs[1] : p.Bs[1]);
     if (p.vec_bc && full) {
-      cp_async16(&sm.bcraw[slot][j][lane], row + t0);
+      cp_async16(&sm.bcraw[slot][r][0], row + t0);
+      cp_async16(&sm.bcraw[slot][r][1], row + t0 + TT / 2);
     } else {
       const long long st = isC ? p.Cs[2] : p.Bs[2];
-      uint4 v;
 #pragma unroll
-      for (int k = 0; k < TT; ++k) {
-        const int t = t0 + k;
-        vec_set<T>(v, k, t < p.seqlen ? ld_f32(row + (long long)t * st) : 0.f);
+      for (int v = 0; v < 2; ++v) {
+        uint4 x;
+#pragma unroll
+        for (int k = 0; k < TT / 2; ++k) {
+          const int t = t0 + v * (TT / 2) + k;
+          vec_set<T>(x, k, t < p.seqlen ? ld_f32(row + (long long)t * st) : 0.f);
+        }
+        sm.bcraw[slot][r][v] = x;
       }
-      sm.bcraw[slot][j][lane] = v;
     }
   }
 }
 
-// Converts the staged raw B/C rows of a tile to fp32 [state pair][step][2] (B pre-multiplied by ln2
-// because delta is carried in the log2 domain), so one LDS.128 broadcast gives a state pair at two steps.
+// Waits until ring slot `slot` holds its tile (TMA: the slot's barrier phase; cp.async: the group).
+MM_DEV void wait_tma_slot(unsigned long long* bar, unsigned& phases, int slot, const Params& p) {
+  const unsigned parity = (phases >> slot) & 1u;
+  if (!mbar_wait_parity_bounded(bar, parity, kSpinLimitNs)) atomicOr(p.err, 2u);
+  phases ^= 1u << slot;
+}
+
+// Converts the staged raw B/C rows of a tile to fp32 [state pair][step][2].
 template <typename T, int NM>
 MM_DEV void convert_bc(WarpSmem<T, NM>& sm, int slot, int lane) {
-  constexpr int TT = Stage<T, NM>::TT;
+  constexpr int HT = Stage<T, NM>::HT;
   constexpr int PS = Stage<T, NM>::PS;
 #pragma unroll
   for (int j = 0; j < Stage<T, NM>::ROWS; ++j) {
@@ -163,44 +204,45 @@ MM_DEV void convert_bc(WarpSmem<T, NM>& sm, int slot, int lane) {
     if (r < 2 * NM) {
       const bool isC = r >= NM;
       const int n = isC ? r - NM : r;
-      const uint4 v = sm.bcraw[slot][j][lane];
       float* dst = sm.bc + (isC ? Stage<T, NM>::COFF : 0) + (n >> 1) * PS + (n & 1);
       const float scale = isC ? 1.0f : kLn2;
 #pragma unroll
-      for (int kp = 0; kp < TT / 2; ++kp) {
-        const float2 e = vec_pair<T>(v, kp);
-        dst[(2 * kp) * 2] = e.x * scale;
-        dst[(2 * kp + 1) * 2] = e.y * scale;
+      for (int v = 0; v < 2; ++v) {
+        const uint4 x = sm.bcraw[slot][r][v];
+#pragma unroll
+        for (int kp = 0; kp < HT / 2; ++kp) {
+          const float2 e = vec_pair<T>(x, kp);
+          const int k = v * HT + 2 * kp;
+          dst[k * 2] = e.x * scale;
+          dst[(k + 1) * 2] = e.y * scale;
+        }
       }
     }
   }
 }
 
-// Runs the recurrence over one staged tile. WY: compute and store y. ST: A has the S4D-real structure.
+// Runs the recurrence over one half tile (HT steps, one 16-byte vector per row) at step offset kb of the
+// staged tile. WY: compute y. ST: A has the S4D-real structure.
 // Phase 1 computes every step's scalars (softplus(delta), exp(delta*A[0]), delta*u, D*u, SiLU(z)) --
-// independent across steps, so their MUFU latencies overlap; phase 2 is the FMA-only recurrence.
+// independent across steps, so their MUFU latencies overlap. Phase 2 runs in sub-tiles of SK steps with
+// the state pairs in the outer loop: for a fixed pair the h update is the only dependency from one step
+// to the next; the decay powers, the B products and the y partial sums of the SK steps are independent.
 template <typename T, int NM, bool SP, bool WY, bool ST, bool FULL>
-MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
-                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
-                         const Params& p, int t0, int lane) {
-  constexpr int TT = Stage<T, NM>::TT;
-  const uint4 tu = sm.io[slot][0][lane];
-  const uint4 td = sm.io[slot][1][lane];
-  uint4 tz = make_uint4(0, 0, 0, 0);
-  if (WY && p.has_z) tz = sm.io[slot][2][lane];
-  const float* sB = sm.bc;
-  const float* sC = sm.bc + Stage<T, NM>::COFF;
-
-  float dk[TT];   // ST: exp(delta*A[0]); general: delta * log2(e)
-  float duk[TT];  // delta * u
-  float yk[TT];   // WY: D * u, then the finished output
-  float gk[TT];   // WY: SiLU(z) (1 without z)
+MM_DEV void compute_half(const uint4& tu, const uint4& td, const uint4& tz, const float* __restrict__ sB,
+                         const float* __restrict__ sC, int kb, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
+                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, bool has_z,
+                         float (&yk)[Stage<T, NM>::HT]) {
+  constexpr int HT = Stage<T, NM>::HT;
+  constexpr int PS = Stage<T, NM>::PS;
+  float dk[HT];   // ST: exp(delta*A[0]); general: delta * log2(e)
+  float duk[HT];  // delta * u
+  float gk[HT];   // WY: SiLU(z) (1 without z)
 #pragma unroll
-  for (int kp = 0; kp < TT / 2; ++kp) {
+  for (int kp = 0; kp < HT / 2; ++kp) {
     const float2 xs = vec_pair<T>(tu, kp);
     const float2 drs = vec_pair<T>(td, kp);
     float2 zs = make_float2(0.f, 0.f);
-    if (WY && p.has_z) zs = vec_pair<T>(tz, kp);
+    if (WY && has_z) zs = vec_pair<T>(tz, kp);
 #pragma unroll
     for (int s2 = 0; s2 < 2; ++s2) {
       const int k = 2 * kp + s2;
@@ -214,17 +256,13 @@ MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2],
       duk[k] = d2 * x;
       if (WY) {
         yk[k] = Dv * x;
-        gk[k] = p.has_z ? silu(s2 ? zs.y : zs.x) : 1.0f;
+        gk[k] = has_z ? silu(s2 ? zs.y : zs.x) : 1.0f;
       }
     }
   }
-  // Phase 2, in sub-tiles of SK steps with the state pairs in the outer loop: for a fixed pair the h
-  // update is the only dependency from one step to the next; the decay powers, the B products and the
-  // y partial sums of the SK steps are independent of each other.
-  constexpr int SK = TT < 4 ? TT : 4;
-  constexpr int PS = Stage<T, NM>::PS;
+  constexpr int SK = HT < 4 ? HT : 4;
 #pragma unroll
-  for (int k0 = 0; k0 < TT; k0 += SK) {
+  for (int k0 = 0; k0 < HT; k0 += SK) {
     f2_t a[SK], rr[SK], du2[SK], dd2[SK], y2[SK];
 #pragma unroll
     for (int j = 0; j < SK; ++j) {
@@ -245,8 +283,8 @@ MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2],
       float4 bq[SK / 2], cq[SK / 2];
 #pragma unroll
       for (int j2 = 0; j2 < SK / 2; ++j2) {
-        bq[j2] = *reinterpret_cast<const float4*>(sB + pi * PS + (k0 + 2 * j2) * 2);
-        if (WY) cq[j2] = *reinterpret_cast<const float4*>(sC + pi * PS + (k0 + 2 * j2) * 2);
+        bq[j2] = *reinterpret_cast<const float4*>(sB + pi * PS + (kb + k0 + 2 * j2) * 2);
+        if (WY) cq[j2] = *reinterpret_cast<const float4*>(sC + pi * PS + (kb + k0 + 2 * j2) * 2);
       }
 #pragma unroll
       for (int j = 0; j < SK; ++j) {
@@ -277,16 +315,40 @@ MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2],
       }
     }
   }
-  if (WY && ln.active) {
-    if (FULL && p.vec_io) {
-      uint4 yv;
+}
+
+template <typename T, int NM, bool SP, bool WY, bool ST>
+MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
+                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
+                         const Params& p, int t0, int lane) {
+  constexpr int HT = Stage<T, NM>::HT;
+  const float* sB = sm.bc;
+  const float* sC = sm.bc + Stage<T, NM>::COFF;
 #pragma unroll
-      for (int kp = 0; kp < TT / 2; ++kp) vec_set_pair<T>(yv, kp, yk[2 * kp], yk[2 * kp + 1]);
-      __stcs(reinterpret_cast<uint4*>(ln.y_row + t0), yv);
-    } else {
+  for (int v = 0; v < 2; ++v) {
+    const int ns = nsteps - v * HT;  // steps of this half inside the range
+    if (ns <= 0) break;
+    const uint4 tu = sm.io[slot][0][lane][v];
+    const uint4 td = sm.io[slot][1][lane][v];
+    uint4 tz = make_uint4(0, 0, 0, 0);
+    if (WY && p.has_z) tz = sm.io[slot][2][lane][v];
+    float yk[HT];
+    if (ns >= HT)
+      compute_half<T, NM, SP, WY, ST, true>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, ns, sum_d2, min_d2, p.has_z, yk);
+    else
+      compute_half<T, NM, SP, WY, ST, false>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, ns, sum_d2, min_d2, p.has_z, yk);
+    if (WY && ln.active) {
+      const int tb = t0 + v * HT;
+      if (ns >= HT && p.vec_io) {
+        uint4 yv;
 #pragma unroll
-      for (int k = 0; k < TT; ++k)
-        if (k < nsteps) st_f32(ln.y_row + (long long)(t0 + k) * p.ys[2], yk[k]);
+        for (int kp = 0; kp < HT / 2; ++kp) vec_set_pair<T>(yv, kp, yk[2 * kp], yk[2 * kp + 1]);
+        __stcs(reinterpret_cast<uint4*>(ln.y_row + tb), yv);
+      } else {
+#pragma unroll
+        for (int k = 0; k < HT; ++k)
+          if (k < ns) st_f32(ln.y_row + (long long)(tb + k) * p.ys[2], yk[k]);
+      }
     }
   }
 }
@@ -295,11 +357,12 @@ MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2],
 // tiles of copies in flight ahead of the one being computed. With `stop_from` < t_end, the loop may end
 // early at a tile boundary t >= stop_from once every lane's slowest-decaying state has decayed below
 // 2^kDecayCutoffLog2 over the range (the recompute after a carry hand-off); returns the end reached.
+// `phases` holds the parity of each TMA ring slot's barrier and persists across calls.
 template <typename T, int NM, bool SP, bool WY, bool ST>
 MM_DEV int run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end, f2_t (&h)[NM / 2],
                      const f2_t (&A2)[NM / 2], float A0, float Dv, float& sum_d2, float& min_d2,
-                     WarpSmem<T, NM>& sm, int lane, int stop_from = INT_MAX, bool decays = false,
-                     float A_max = 0.f) {
+                     WarpSmem<T, NM>& sm, int lane, unsigned& phases, int stop_from = INT_MAX,
+                     bool decays = false, float A_max = 0.f) {
   constexpr int TT = Stage<T, NM>::TT;
   if (t_begin >= t_end) return t_end;
   const int ntiles = (t_end - t_begin + TT - 1) / TT;
@@ -307,32 +370,36 @@ MM_DEV int run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end,
 #pragma unroll
   for (int i = 0; i < kStages - 1; ++i) {
     if (i < ntiles) issue_tile<T, NM>(sm, i, p, ln, t_begin + i * TT, lane);
-    cp_async_commit();
+    if (!p.use_tma) cp_async_commit();
   }
   int t_done = t_end;
   for (int i = 0; i < ntiles; ++i) {
     const int nx = i + kStages - 1;
     if (nx < ntiles) issue_tile<T, NM>(sm, nx % kStages, p, ln, t_begin + nx * TT, lane);
-    cp_async_commit();
-    cp_async_wait<kStages - 1>();
-    __syncwarp();
     const int slot = i % kStages;
+    if (p.use_tma) {
+      wait_tma_slot(&sm.bar[slot], phases, slot, p);
+    } else {
+      cp_async_commit();
+      cp_async_wait<kStages - 1>();
+    }
+    __syncwarp();
     convert_bc<T, NM>(sm, slot, lane);
     __syncwarp();
     const int t0 = t_begin + i * TT;
-    const int nsteps = min(TT, t_end - t0);
-    if (nsteps == TT)
-      compute_tile<T, NM, SP, WY, ST, true>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
-    else
-      compute_tile<T, NM, SP, WY, ST, false>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
+    compute_tile<T, NM, SP, WY, ST>(sm, slot, h, A2, A0, Dv, min(TT, t_end - t0), sum_d2, min_d2, ln, p, t0, lane);
     __syncwarp();  // B/C buffer and this slot are free for the next iteration
     if (t0 + TT >= stop_from && t0 + TT < t_end &&
         __all_sync(0xffffffffu, decays && (A_max * sum_d2 <= kDecayCutoffLog2))) {
       t_done = t0 + TT;
+      // drain the tiles already issued beyond this one so the ring's barrier phases stay in step
+      if (p.use_tma) {
+        for (int j = i + 1; j < min(i + kStages, ntiles); ++j) wait_tma_slot(&sm.bar[j % kStages], phases, j % kStages, p);
+      }
       break;
     }
   }
-  cp_async_wait<0>();
+  if (!p.use_tma) cp_async_wait<0>();
   __syncwarp();
   return t_done;
 }
@@ -394,11 +461,12 @@ MM_DEV void publish_flag(const Params& p, int w, unsigned v, int lane) {
 
 template <typename T, int NM, bool SP, bool ST>
 MM_DEV void process_piece(const Params& p, int w, int g, int tile_lo, int tile_hi, bool first_piece,
-                          WarpSmem<T, NM>& sm, int lane) {
+                          WarpSmem<T, NM>& sm, int lane, unsigned& phases) {
   constexpr int TT = Stage<T, NM>::TT;
   Lane<T> ln;
   ln.b = g / p.groups_per_batch;
   const int dg = g % p.groups_per_batch;
+  ln.dg = dg;
   ln.d = dg * 32 + lane;
   ln.active = ln.d < p.dim;
   const int dd = ln.active ? ln.d : p.dim - 1;
@@ -438,7 +506,7 @@ MM_DEV void process_piece(const Params& p, int w, int g, int tile_lo, int tile_h
   float acc = 0.f, min_d2 = INFINITY;
 
   // Pass 1 over the head: state only (its y is produced by the exact recompute below).
-  run_range<T, NM, SP, false, ST>(p, ln, t_lo, head_end, h, A2, A0, Dv, acc, min_d2, sm, lane);
+  run_range<T, NM, SP, false, ST>(p, ln, t_lo, head_end, h, A2, A0, Dv, acc, min_d2, sm, lane, phases);
 
   // Then one loop over the y-producing ranges: the rest of pass 1, and (for pieces that start
   // mid-sequence) the recompute from the true incoming state once the look-back has produced it.
@@ -448,7 +516,7 @@ MM_DEV void process_piece(const Params& p, int w, int g, int tile_lo, int tile_h
   const bool decays = A_max < 0.f;
   for (;;) {
     const int t_end_reached =
-        run_range<T, NM, SP, true, ST>(p, ln, t, t_hi, h, A2, A0, Dv, acc, min_d2, sm, lane,
+        run_range<T, NM, SP, true, ST>(p, ln, t, t_hi, h, A2, A0, Dv, acc, min_d2, sm, lane, phases,
                                        recompute ? head_end : INT_MAX,
                                        decays && (SP || min_d2 >= 0.f), A_max);
     if (recompute) {
@@ -538,7 +606,7 @@ MM_DEV void process_piece(const Params& p, int w, int g, int tile_lo, int tile_h
 }
 
 template <typename T, int NM, bool SP, bool ST>
-MM_DEV void scan_warp(const Params& p, int w, WarpSmem<T, NM>& sm, int lane) {
+MM_DEV void scan_warp(const Params& p, int w, WarpSmem<T, NM>& sm, int lane, unsigned& phases) {
   const long long tpr = p.tiles_per_row;
   const long long f0 = (long long)w * p.tiles_per_warp;
   const long long f1 = min(f0 + p.tiles_per_warp, p.total_tiles);
@@ -549,13 +617,14 @@ MM_DEV void scan_warp(const Params& p, int w, WarpSmem<T, NM>& sm, int lane) {
   for (int g = g_hi; g >= g_lo; --g) {
     const int tile_lo = (int)(max(f0, (long long)g * tpr) - (long long)g * tpr);
     const int tile_hi = (int)(min(f1, (long long)(g + 1) * tpr) - (long long)g * tpr);
-    process_piece<T, NM, SP, ST>(p, w, g, tile_lo, tile_hi, g == g_hi, sm, lane);
+    process_piece<T, NM, SP, ST>(p, w, g, tile_lo, tile_hi, g == g_hi, sm, lane, phases);
   }
 }
 
 template <typename T, int NM, bool SP>
-__global__ void __launch_bounds__(kWarpsPerCta * 32, NM <= 16 ? MM_SCAN_MIN_BLOCKS : 2) scan_kernel(const Params p) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+__global__ void __launch_bounds__(kWarpsPerCta * 32, NM <= 16 ? MM_SCAN_MIN_BLOCKS : 2)
+    scan_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   unsigned w = 0;
@@ -563,6 +632,12 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, NM <= 16 ? MM_SCAN_MIN_BLOC
   w = __shfl_sync(0xffffffffu, w, 0);
   if ((int)w >= p.n_warps) return;
   WarpSmem<T, NM>& sm = reinterpret_cast<WarpSmem<T, NM>*>(smem_raw)[wib];
+  if (p.use_tma && lane == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&sm.bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  unsigned phases = 0;
 
   // S4D-real structure check for the channels of this warp's pieces (A[d,n] = (n+1) A[d,0], to 4 ulp).
   // The decision must be uniform over the warp; channels of different groups are checked piecewise.
@@ -581,9 +656,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, NM <= 16 ? MM_SCAN_MIN_BLOC
   }
   st = __all_sync(0xffffffffu, st);
   if (st)
-    scan_warp<T, NM, SP, true>(p, (int)w, sm, lane);
+    scan_warp<T, NM, SP, true>(p, (int)w, sm, lane, phases);
   else
-    scan_warp<T, NM, SP, false>(p, (int)w, sm, lane);
+    scan_warp<T, NM, SP, false>(p, (int)w, sm, lane, phases);
 }
 
 template <typename T, int NM, bool SP>

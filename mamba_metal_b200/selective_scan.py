@@ -27,12 +27,15 @@ def _scan_dtype(*ts) -> torch.dtype:
     return torch.float32
 
 
-def selective_scan_into(u, delta, A, B, C, D, z, y, state_out, delta_softplus: bool, piece_tiles: int = 0):
+def selective_scan_into(u, delta, A, B, C, D, z, y, state_out, delta_softplus: bool, piece_tiles: int = 0,
+                        use_tma: bool = True):
     """Runs the scan kernel on given (possibly strided) views and writes into ``y`` / ``state_out``.
 
     u, delta, z, y: (batch, dim, seqlen) views with any strides (channel-first and channels-last both
     work); B, C: (batch, dstate, seqlen) views; A: (dim, dstate) float32; D: (dim,) float32 or None;
     state_out: contiguous float32 (batch, dim, dstate) or None. All activation views share one dtype.
+    ``piece_tiles`` (0 = automatic) sets the timestep tiles per warp; ``use_tma=False`` stages tiles with
+    cp.async / plain loads even where TMA applies. Returns the workspace tensor (for status queries).
     """
     dev = _lib.require_cuda(u, delta, A, B, C, D, z, y, state_out)
     lib = _lib.lib()
@@ -52,6 +55,7 @@ def selective_scan_into(u, delta, A, B, C, D, z, y, state_out, delta_softplus: b
     args.A_stride = (ctypes.c_int64 * 2)(*A.stride())
     args.delta_softplus = int(bool(delta_softplus))
     args.piece_tiles = int(piece_tiles)
+    args.options = 0 if use_tma else 1
     nbytes = ctypes.c_size_t(0)
     _lib.check(lib.mm_selective_scan_workspace_size(ctypes.byref(args), ctypes.byref(nbytes)),
                "mm_selective_scan_workspace_size")

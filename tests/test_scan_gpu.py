@@ -98,11 +98,12 @@ def test_config0_golden(golden_dir):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("shape", [(1, 1, 1), (1, 3, 7), (2, 5, 31), (1, 33, 33), (3, 40, 1023), (1, 64, 1025),
-                                   (2, 17, 4097)])
-def test_odd_shapes(dtype, shape):
+                                   (2, 17, 4097), (2, 48, 4096)])
+@pytest.mark.parametrize("use_tma", [True, False])
+def test_odd_shapes(dtype, shape, use_tma):
     b, d, L = shape
     inp = R.make_baseline_inputs(b, d, 16, L, seed=L + d)
-    y, h = run(inp, dtype)
+    y, h = _into(inp, dtype, use_tma=use_tma)
     q = {k: (torch.as_tensor(v).to(dtype).float().numpy() if k in ("u", "delta", "B", "C", "z") else v)
          for k, v in inp.items()}
     yr, hr = R.selective_scan_vec(q["u"], q["delta"], q["A"], q["B"], q["C"], q["D"], q["z"], delta_softplus=True,
@@ -114,18 +115,20 @@ def test_odd_shapes(dtype, shape):
 
 @pytest.mark.parametrize("piece_tiles", [1, 2, 3, 5, 16])
 @pytest.mark.parametrize("general_A", [False, True])
-def test_small_pieces_lookback(piece_tiles, general_A):
-    """Forces many warps per sequence, so carries pass through long look-back chains."""
+@pytest.mark.parametrize("use_tma", [True, False])
+def test_small_pieces_lookback(piece_tiles, general_A, use_tma):
+    """Forces many warps per sequence, so carries pass through long look-back chains (TMA and
+    cp.async staging)."""
     inp = R.make_baseline_inputs(2, 70, 16, 2000, seed=7)
     if general_A:
         inp["A"] = -np.random.default_rng(1).uniform(0.1, 2.0, size=(70, 16)).astype(np.float32)
-    out = _into(inp, torch.float32, piece_tiles)
+    out = _into(inp, torch.float32, piece_tiles, use_tma=use_tma)
     yr, hr = R.selective_scan_vec(**inp, delta_softplus=True, return_state=True, dtype=np.float64)
     assert_close(out[0], yr, RTOL["float32"], f"pieces={piece_tiles} general={general_A} y")
     assert_close(out[1], hr, RTOL["float32"], f"pieces={piece_tiles} general={general_A} state")
 
 
-def _into(inp, dtype, piece_tiles=0, sp=True, channels_last=False):
+def _into(inp, dtype, piece_tiles=0, sp=True, channels_last=False, use_tma=True):
     b, d, L = inp["u"].shape
     n = inp["A"].shape[1]
     t = lambda k: T(inp[k], dtype)
@@ -137,7 +140,8 @@ def _into(inp, dtype, piece_tiles=0, sp=True, channels_last=False):
         u, de, z, Bm, Cm = t("u"), t("delta"), t("z"), t("B"), t("C")
         y = torch.empty((b, d, L), dtype=dtype, device=DEV)
     h = torch.empty((b, d, n), dtype=torch.float32, device=DEV)
-    ws = selective_scan_into(u, de, T(inp["A"]), Bm, Cm, T(inp["D"]), z, y, h, sp, piece_tiles=piece_tiles)
+    ws = selective_scan_into(u, de, T(inp["A"]), Bm, Cm, T(inp["D"]), z, y, h, sp, piece_tiles=piece_tiles,
+                             use_tma=use_tma)
     rc = _lib.lib().mm_selective_scan_status(ws.data_ptr(), _lib.stream_handle(torch.device(DEV)))
     assert rc == 0, f"carry hand-off status {rc}"
     return y, h
