@@ -50,7 +50,8 @@ enum {
   MM_ERR_DTYPE = -3,     /* unknown dtype code */
   MM_ERR_WORKSPACE = -4, /* workspace missing, too small or not 256-byte aligned */
   MM_ERR_LAUNCH = -5,    /* the CUDA launch (or the workspace clear) failed */
-  MM_ERR_TIMEOUT = -6    /* a carry hand-off between warps waited past its limit (status only) */
+  MM_ERR_TIMEOUT = -6,   /* a carry hand-off between warps waited past its limit (status only) */
+  MM_ERR_TOO_LARGE = -7  /* the call needs more scratch than the fixed buffer of the no-allocation entry */
 };
 
 /* Largest dstate the scan and the decode step accept (same limit as the reference,
@@ -103,6 +104,20 @@ typedef struct MMScanArgs {
 int mm_selective_scan_workspace_size(const MMScanArgs* args, size_t* bytes);
 int mm_selective_scan_fwd(const MMScanArgs* args, void* workspace, size_t workspace_bytes,
                           mm_stream_t stream);
+/* Allocation-free variant of mm_selective_scan_fwd, for callers that cannot allocate device memory:
+ * for example a host that runs inside a fixed memory budget carved out up front by another allocator,
+ * or an FFI host (JNI, cgo, a real-time serving loop) whose policy forbids device allocation after
+ * start-up. Instead of a caller-provided workspace it uses a scratch buffer of
+ * MM_SCAN_NOALLOC_SCRATCH_BYTES that is a static __device__ array of this library: every GPU that loads
+ * the library holds it until the process exits. The caller still provides every input and output.
+ * Calls whose workspace would exceed the buffer return MM_ERR_TOO_LARGE without launching anything.
+ * The first call on a device looks up the buffer's device address (cudaGetSymbolAddress, once per
+ * device); make that first call before any stream capture. All calls share the one buffer, so calls
+ * that overlap in time on the GPU (other streams, other host threads) race and must be serialised by
+ * the caller; each call clears the part of the buffer that must start at zero. No counterpart exists in
+ * the reference (its Metal kernel needs no workspace). */
+#define MM_SCAN_NOALLOC_SCRATCH_BYTES (16u << 20)
+int mm_selective_scan_fwd_noalloc(const MMScanArgs* args, mm_stream_t stream);
 /* Synchronises `stream` and reports MM_OK or MM_ERR_TIMEOUT for the last scan that used
  * `workspace`. Diagnostics only; the scan itself never blocks the host. */
 int mm_selective_scan_status(const void* workspace, mm_stream_t stream);

@@ -22,8 +22,9 @@ DTYPE_CODE = {torch.float32: MM_F32, torch.float16: MM_F16, torch.bfloat16: MM_B
 
 ERROR_NAMES = {
     0: "MM_OK", -1: "MM_ERR_ARG", -2: "MM_ERR_SHAPE", -3: "MM_ERR_DTYPE",
-    -4: "MM_ERR_WORKSPACE", -5: "MM_ERR_LAUNCH", -6: "MM_ERR_TIMEOUT",
+    -4: "MM_ERR_WORKSPACE", -5: "MM_ERR_LAUNCH", -6: "MM_ERR_TIMEOUT", -7: "MM_ERR_TOO_LARGE",
 }
+MM_SCAN_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 _i64 = ctypes.c_int64
 _p = ctypes.c_void_p
@@ -74,6 +75,7 @@ class MMAddNormArgs(ctypes.Structure):
 _SIGNATURES = {
     "mm_selective_scan_workspace_size": ([ctypes.POINTER(MMScanArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "mm_selective_scan_fwd": ([ctypes.POINTER(MMScanArgs), _p, ctypes.c_size_t, _p], ctypes.c_int),
+    "mm_selective_scan_fwd_noalloc": ([ctypes.POINTER(MMScanArgs), _p], ctypes.c_int),
     "mm_selective_scan_status": ([_p, _p], ctypes.c_int),
     "mm_selective_scan_stats": ([_p, ctypes.POINTER(ctypes.c_ulonglong), _p], ctypes.c_int),
     "mm_causal_conv1d_fwd": ([ctypes.POINTER(MMConvArgs), _p], ctypes.c_int),

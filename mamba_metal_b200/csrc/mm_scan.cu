@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "mm_scan.cuh"
 
@@ -211,4 +212,41 @@ extern "C" int mm_selective_scan_status(const void* ws, mm_stream_t stream) {
     return MM_ERR_LAUNCH;
   if (cudaStreamSynchronize(s) != cudaSuccess) return MM_ERR_LAUNCH;
   return err ? MM_ERR_TIMEOUT : MM_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free entry point: the workspace is a fixed static __device__ array of this library.
+
+namespace {
+__device__ __align__(256) unsigned char g_scan_scratch[MM_SCAN_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_scan_scratch on the current device, looked up once per device. The symbol's
+// name in host code is only a host-side handle; kernels must be given this address.
+int scratch_for_current_device(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MM_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_scan_scratch) != cudaSuccess || p == nullptr) return MM_ERR_LAUNCH;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return MM_OK;
+}
+}  // namespace
+
+extern "C" int mm_selective_scan_fwd_noalloc(const MMScanArgs* a, mm_stream_t stream) {
+  size_t need = 0;
+  const int rc = mm_selective_scan_workspace_size(a, &need);
+  if (rc != MM_OK) return rc;
+  if (need > MM_SCAN_NOALLOC_SCRATCH_BYTES) return MM_ERR_TOO_LARGE;
+  void* ws = nullptr;
+  const int rs = scratch_for_current_device(&ws);
+  if (rs != MM_OK) return rs;
+  return mm_selective_scan_fwd(a, ws, MM_SCAN_NOALLOC_SCRATCH_BYTES, stream);
 }
