@@ -184,6 +184,7 @@ def run_reference(args, rank, world):
 
 
 def run_ours(args, rank, world, local_rank):
+    """configs[1] selective scan (the default workload)."""
     import torch
     import torch.distributed as dist
 
@@ -296,6 +297,159 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def _dist_tools(dev, world):
+    import torch
+    import torch.distributed as dist
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    return sync_all, max_over_ranks
+
+
+def run_conv(args, rank, world, local_rank):
+    """configs[1] causal conv1d: fp16 x (8, 1536, 4096) channel-first, w (1536, 4) ~ U(-.5,.5),
+    bias ~ U(-.1,.1), no activation (BASELINE states none); every rank runs the same batch (weak)."""
+    import torch
+
+    from mamba_metal_b200 import causal_conv1d
+    from oracle.scan_ref import make_conv_inputs
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    sync_all, max_over_ranks = _dist_tools(dev, world)
+    b, dm, L = CFG["batch"], CFG["dim"], CFG["seqlen"]
+    ci = make_conv_inputs(b, dm, L, seed=0)
+    x = torch.from_numpy(ci["x"]).to(dev, torch.float16)
+    w = torch.from_numpy(ci["weight"]).to(dev)
+    bias = torch.from_numpy(ci["bias"]).to(dev)
+    out = torch.empty_like(x)
+    for _ in range(args.warmup):
+        causal_conv1d(x, w, bias, silu=False, out=out)
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(_nvml_index(local_rank)) as clk:
+        sync_all()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            causal_conv1d(x, w, bias, silu=False, out=out)
+        e1.record(stream)
+        sync_all()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    if rank != 0:
+        return
+    elems = b * dm * L
+    nbytes = 2 * 2 * elems + 4 * dm * 5
+    peak, kind = load_peaks()
+    ach = nbytes / (ms * 1e-3) / 1e9
+    print(json.dumps({"metric": "causal conv1d Gelem/s (configs[1])", "value": world * elems / (ms * 1e-3) / 1e9,
+                      "unit": "Gelem/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "f16 in / f32 math", "data": "synthetic (BASELINE configs[1] conv distributions, seed 0)",
+                      "config": {"workload": "causal_conv1d configs[1], channel-first, width 4, no activation",
+                                 "batch": b, "dim": dm, "seqlen": L, "l2": "inputs larger than L2"},
+                      "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                                   "traffic": None, "peak_kind": kind, "algorithmic_bytes": nbytes},
+                      "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
+
+
+DECODE = dict(d_model=2560, n_layer=64, vocab_size=50280, d_state=16, d_conv=4, expand=2, dt_rank=160,
+              batch=64, prompt=2048, new_tokens=256)
+
+
+def decode_bytes_per_step(world):
+    """HBM bytes one decode step must move per GPU: bf16 weights of every layer (sharded over the
+    tensor-parallel ranks) + the tied head (replicated) + fp32 SSM and conv state read and written."""
+    c = DECODE
+    E, dm, R, N, V, B = c["expand"] * c["d_model"], c["d_model"], c["dt_rank"], c["d_state"], c["vocab_size"], c["batch"]
+    per_layer_w = 2 * (dm * 2 * E + E * (R + 2 * N) + R * E + E + E * dm) + 4 * (E * 5 + E * N + E)
+    state = 2 * 4 * B * E * (N + c["d_conv"])
+    return c["n_layer"] * (per_layer_w + state) / world + 2 * V * dm
+
+
+def run_decode(args, rank, world, local_rank):
+    """Mamba-2.8b architecture (64 layers, d_model 2560, d_inner 5120, N 16, dt_rank 160,
+    vocab 50280), random init (seed 0), bf16 weights with fp32 state, batch 64, 2,048-token prompts of
+    uniform random ids, parallel prefill, then greedy decode with the CUDA-graph step; tensor-parallel over
+    d_inner at N > 1 (two fp32 all-reduces per layer). One step = one token for all 64 sequences."""
+    import torch
+
+    from mamba_metal_b200 import GraphDecoder, MambaConfig, MambaModel, generate_ids, init_weights_
+    from mamba_metal_b200.parallel import tp_model
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    sync_all, max_over_ranks = _dist_tools(dev, world)
+    c = DECODE
+    cfg = MambaConfig(d_model=c["d_model"], n_layer=c["n_layer"], vocab_size=c["vocab_size"], d_state=c["d_state"],
+                      d_conv=c["d_conv"], expand=c["expand"], dt_rank=c["dt_rank"])
+    with torch.no_grad():
+        model = init_weights_(MambaModel(cfg, dtype=torch.bfloat16, device=dev), seed=0)
+        if world > 1:
+            model = tp_model(model, rank, world)
+            torch.cuda.empty_cache()
+    ids_host = torch.randint(0, c["vocab_size"], (c["batch"], c["prompt"]),
+                             generator=torch.Generator().manual_seed(0)).pin_memory()
+    ids = ids_host.to(dev)
+    with torch.no_grad():
+        logits, conv, ssm = model.prefill(ids, last_only=True)
+        first = torch.argmax(logits[:, -1], dim=-1)
+        dec = GraphDecoder(model, conv, ssm, first)
+        for _ in range(args.warmup):
+            dec.step()
+        stream = torch.cuda.current_stream(dev)
+        with ClockSampler(_nvml_index(local_rank)) as clk:
+            sync_all()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                dec.step()
+            e1.record(stream)
+            sync_all()
+        ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        del dec
+        # e2e: prompt ids from pinned host memory, prefill + new_tokens greedy steps, ids read back
+        n_new = c["new_tokens"]
+        sync_all()
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        out_host = torch.empty((c["batch"], n_new), dtype=torch.long).pin_memory()
+        e2.record(stream)
+        out = generate_ids(model, ids_host.to(dev, non_blocking=True), n_new)
+        out_host.copy_(out, non_blocking=True)
+        e3.record(stream)
+        sync_all()
+        e2e_ms = max_over_ranks(e2.elapsed_time(e3))
+    if rank != 0:
+        return
+    peak, kind = load_peaks()
+    nbytes = decode_bytes_per_step(world)
+    ach = nbytes / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": METRIC, "value": c["batch"] / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 weights / fp32 state", "data": "synthetic (uniform random prompt ids, "
+        "random-init weights, seed 0)",
+        "config": {"workload": "decode configs[3]: Mamba-2.8b architecture, batch 64, prompt 2048, greedy, CUDA graph",
+                   **{k: c[k] for k in ("d_model", "n_layer", "batch", "prompt")}, "parallelism": f"tp{world}"},
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                     "traffic": None, "peak_kind": kind, "algorithmic_bytes": nbytes},
+        "e2e": {"value": c["batch"] * n_new / (e2e_ms * 1e-3), "unit": "tok/s", "ms": e2e_ms,
+                "h2d_bytes_per_step": ids_host.numel() * 8 / n_new, "d2h_bytes_per_step": c["batch"] * 8,
+                "note": "prompt H2D + prefill + 256 greedy steps + ids D2H, per generated token"},
+        # libmamba_b200 kernels per step: conv step, SSM step and residual-norm per layer, plus the first norm
+        "gpu_launches": args.steps * (3 * c["n_layer"] + 1), "clocks": clk.summary()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -303,6 +457,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="device loop only: no e2e arm, no CPU baseline")
+    ap.add_argument("--workload", choices=["scan", "conv", "decode"], default="scan",
+                    help="scan: configs[1] selective scan (default, the headline); conv: configs[1] causal conv1d; "
+                         "decode: configs[3] Mamba-2.8b-architecture batch-64 decode, tensor-parallel at N > 1")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -320,7 +477,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        {"scan": run_ours, "conv": run_conv, "decode": run_decode}[args.workload](args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -49,11 +49,11 @@ class RMSNorm(nn.Module):
 class MambaResidualBlock(nn.Module):
     """Pre-norm + residual wrapper around a MambaBlock (mamba_model.py:35-58)."""
 
-    def __init__(self, cfg: MambaConfig, dtype: torch.dtype = torch.float32, device=None):
+    def __init__(self, cfg: MambaConfig, dtype: torch.dtype = torch.float32, device=None, tp_world: int = 1):
         super().__init__()
         self.norm = RMSNorm(cfg.d_model, eps=cfg.rms_norm_eps, device=device)
         self.mixer = MambaBlock(cfg.d_model, cfg.d_state, cfg.d_conv, cfg.expand, cfg.dt_rank, dtype=dtype,
-                                device=device)
+                                device=device, tp_world=tp_world)
 
     def forward(self, x):
         return x + self.mixer(self.norm(x))
@@ -70,17 +70,20 @@ class MambaResidualBlock(nn.Module):
 class MambaModel(nn.Module):
     """Stack of MambaResidualBlocks with a tied LM head (mamba_model.py:61-127)."""
 
-    def __init__(self, cfg: MambaConfig, dtype: torch.dtype = torch.float32, device=None):
+    def __init__(self, cfg: MambaConfig, dtype: torch.dtype = torch.float32, device=None, tp_world: int = 1):
         super().__init__()
         self.cfg = cfg
         self.dtype = dtype
+        self.tp_world = tp_world
         self.embeddings = nn.Embedding(cfg.vocab_size, cfg.d_model, dtype=dtype, device=device)
-        self.layers = nn.ModuleList([MambaResidualBlock(cfg, dtype=dtype, device=device) for _ in range(cfg.n_layer)])
+        self.layers = nn.ModuleList([MambaResidualBlock(cfg, dtype=dtype, device=device, tp_world=tp_world)
+                                     for _ in range(cfg.n_layer)])
         self.norm_f = RMSNorm(cfg.d_model, eps=cfg.rms_norm_eps, device=device)
 
     @property
     def d_inner(self) -> int:
-        return self.cfg.expand * self.cfg.d_model
+        """Inner channels held by this model (all of them, or this rank's slice under tensor parallelism)."""
+        return self.cfg.expand * self.cfg.d_model // self.tp_world
 
     def _norm_weight(self, i: int) -> torch.Tensor:
         return self.layers[i].norm.weight if i < len(self.layers) else self.norm_f.weight

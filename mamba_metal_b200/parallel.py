@@ -1,0 +1,85 @@
+"""Tensor parallelism over d_inner for MambaModel (one process per GPU, torch.distributed).
+
+Each rank holds a contiguous 1/world slice of every layer's inner channels:
+
+- in_proj  : the x-half rows and the z-half rows of its channel slice (column-parallel);
+- conv1d, dt_proj (weight rows + bias), A_log, D: its channel slice;
+- x_proj   : the columns of its channel slice (row-parallel) -> partial (B, dt_rank + 2N), all-reduced;
+- out_proj : the columns of its channel slice (row-parallel) -> partial (B, d_model), all-reduced;
+- embeddings, RMSNorm weights and the tied head: replicated.
+
+Mamba-1's x_proj reads every inner channel, so a layer needs two all-reduces (after x_proj and after
+out_proj); the scan, the conv and the decode step themselves need no communication. The partial sums are
+reduced in float32. The reference has no multi-device code; this is the configs[3] layout of the
+B200 build.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from mamba_metal_b200.mamba_model import MambaConfig, MambaModel
+
+
+def channel_range(d_inner: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous inner-channel slice [lo, hi) of `rank` (d_inner must divide evenly)."""
+    if d_inner % world:
+        raise ValueError(f"d_inner {d_inner} is not divisible by the tensor-parallel size {world}")
+    per = d_inner // world
+    return rank * per, (rank + 1) * per
+
+
+def shard_state_dict(sd: dict, cfg: MambaConfig, rank: int, world: int) -> dict:
+    """Slices a full MambaModel state_dict for one tensor-parallel rank (pure tensor indexing)."""
+    d_inner = cfg.expand * cfg.d_model
+    lo, hi = channel_range(d_inner, rank, world)
+    out = {}
+    for k, v in sd.items():
+        if ".mixer." not in k:
+            out[k] = v
+            continue
+        name = k.split(".mixer.", 1)[1]
+        if name == "in_proj.weight":
+            out[k] = torch.cat([v[lo:hi], v[d_inner + lo:d_inner + hi]], dim=0)
+        elif name in ("conv1d.weight", "conv1d.bias", "dt_proj.weight", "dt_proj.bias", "A_log", "D"):
+            out[k] = v[lo:hi]
+        elif name in ("x_proj.weight", "out_proj.weight"):
+            out[k] = v[:, lo:hi]
+        else:
+            raise KeyError(k)
+    return {k: v.contiguous() for k, v in out.items()}
+
+
+class _AllReduce:
+    """Sums a partial projection output over the tensor-parallel group, in float32."""
+
+    def __init__(self, group):
+        self.group = group
+
+    def __call__(self, t: torch.Tensor) -> torch.Tensor:
+        if t.dtype == torch.float32:
+            t = t.contiguous()
+            dist.all_reduce(t, group=self.group)
+            return t
+        t32 = t.float()
+        dist.all_reduce(t32, group=self.group)
+        return t32.to(t.dtype)
+
+
+def tp_model(full: MambaModel, rank: int, world: int, group=None) -> MambaModel:
+    """Builds this rank's tensor-parallel MambaModel from a full one (same device and dtype).
+
+    The returned model holds the local channel slice in every mixer and all-reduces after x_proj and
+    after out_proj; its forward / prefill / step / generation API is unchanged (conv and SSM states
+    are per-rank slices of d_inner)."""
+    cfg = full.cfg
+    dev = full.embeddings.weight.device
+    sd = shard_state_dict(full.state_dict(), cfg, rank, world)
+    with torch.device("meta"):
+        local = MambaModel(cfg, dtype=full.dtype, tp_world=world)
+    local = local.to_empty(device=dev)
+    local.load_state_dict(sd, strict=True)
+    reduce = _AllReduce(group)
+    for layer in local.layers:
+        layer.mixer.tp_reduce = reduce
+    return local
