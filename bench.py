@@ -104,6 +104,8 @@ class ClockSampler:
                 self._stop.wait(0.002)
 
         self._thread = threading.Thread(target=loop, daemon=True)
+        self._switch = sys.getswitchinterval()
+        sys.setswitchinterval(0.0002)  # let the sampler thread run between the launching thread's calls
         self._thread.start()
         return self
 
@@ -111,6 +113,7 @@ class ClockSampler:
         if self._thread is not None:
             self._stop.set()
             self._thread.join(timeout=2)
+            sys.setswitchinterval(self._switch)
 
     def summary(self):
         if self._nvml is None or not self.samples:

@@ -1,0 +1,70 @@
+"""Tensor-parallel model over 2 GPUs (NCCL) against the same model on one GPU. Needs >= 2 GPUs; skipped
+otherwise. Each rank runs in its own spawned process; failures are reported through a queue."""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from mamba_metal_b200 import MambaConfig, MambaModel, generate_ids, init_weights_
+    from mamba_metal_b200.parallel import tp_model
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        torch.backends.cuda.matmul.allow_tf32 = False
+        cfg = MambaConfig(d_model=256, n_layer=3, vocab_size=997, dt_rank=16)
+        full = init_weights_(MambaModel(cfg, device=dev), seed=7)
+        ids = torch.randint(0, cfg.vocab_size, (4, 37), generator=torch.Generator().manual_seed(2)).to(dev)
+        with torch.no_grad():
+            ref_logits = full(ids)
+            _, ref_conv, ref_ssm = full.prefill(ids)
+            ref_out = generate_ids(full, ids, 8)
+            tp = tp_model(full, rank, world)
+            logits = tp(ids)
+            _, conv, ssm = tp.prefill(ids)
+            out = generate_ids(tp, ids, 8)
+        lo = rank * tp.d_inner
+        ok_logits = torch.allclose(logits, ref_logits, rtol=1e-4, atol=1e-4 * float(ref_logits.abs().mean()))
+        ok_state = torch.allclose(ssm[1], ref_ssm[1][:, lo:lo + tp.d_inner], rtol=1e-4, atol=1e-5)
+        ok_conv = torch.allclose(conv[2], ref_conv[2][:, lo:lo + tp.d_inner], rtol=1e-5, atol=1e-6)
+        same_tokens = bool(torch.equal(out, ref_out))
+        q.put((rank, ok_logits, ok_state, ok_conv, same_tokens, float((logits - ref_logits).abs().max())))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, False, False, False, False, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_matches_single_gpu():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[1] and r[2] and r[3] and r[4] for r in res), res
