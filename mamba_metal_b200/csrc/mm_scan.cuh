@@ -317,40 +317,59 @@ MM_DEV void compute_half(const uint4& tu, const uint4& td, const uint4& tz, cons
   }
 }
 
-template <typename T, int NM, bool SP, bool WY, bool ST>
-MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
-                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
-                         const Params& p, int t0, int lane) {
+// One staged tile = two half tiles. A full tile (the common case) is one branch-free block, so the
+// scheduler can overlap the second half's MUFU-heavy phase 1 with the first half's FMA-heavy phase 2.
+template <typename T, int NM, bool SP, bool WY, bool ST, bool FULLTILE>
+MM_DEV void compute_tile_t(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
+                           float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
+                           const Params& p, int t0, int lane) {
   constexpr int HT = Stage<T, NM>::HT;
   const float* sB = sm.bc;
   const float* sC = sm.bc + Stage<T, NM>::COFF;
+  float yk[2][HT];
 #pragma unroll
   for (int v = 0; v < 2; ++v) {
     const int ns = nsteps - v * HT;  // steps of this half inside the range
-    if (ns <= 0) break;
+    if (!FULLTILE && ns <= 0) break;
     const uint4 tu = sm.io[slot][0][lane][v];
     const uint4 td = sm.io[slot][1][lane][v];
     uint4 tz = make_uint4(0, 0, 0, 0);
     if (WY && p.has_z) tz = sm.io[slot][2][lane][v];
-    float yk[HT];
-    if (ns >= HT)
-      compute_half<T, NM, SP, WY, ST, true>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, ns, sum_d2, min_d2, p.has_z, yk);
+    if (FULLTILE || ns >= HT)
+      compute_half<T, NM, SP, WY, ST, true>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, HT, sum_d2, min_d2, p.has_z,
+                                           yk[v]);
     else
-      compute_half<T, NM, SP, WY, ST, false>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, ns, sum_d2, min_d2, p.has_z, yk);
-    if (WY && ln.active) {
+      compute_half<T, NM, SP, WY, ST, false>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, ns, sum_d2, min_d2, p.has_z,
+                                            yk[v]);
+  }
+  if (WY && ln.active) {
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      const int ns = nsteps - v * HT;
+      if (!FULLTILE && ns <= 0) break;
       const int tb = t0 + v * HT;
-      if (ns >= HT && p.vec_io) {
+      if ((FULLTILE || ns >= HT) && p.vec_io) {
         uint4 yv;
 #pragma unroll
-        for (int kp = 0; kp < HT / 2; ++kp) vec_set_pair<T>(yv, kp, yk[2 * kp], yk[2 * kp + 1]);
+        for (int kp = 0; kp < HT / 2; ++kp) vec_set_pair<T>(yv, kp, yk[v][2 * kp], yk[v][2 * kp + 1]);
         __stcs(reinterpret_cast<uint4*>(ln.y_row + tb), yv);
       } else {
 #pragma unroll
         for (int k = 0; k < HT; ++k)
-          if (k < ns) st_f32(ln.y_row + (long long)(tb + k) * p.ys[2], yk[k]);
+          if (k < ns) st_f32(ln.y_row + (long long)(tb + k) * p.ys[2], yk[v][k]);
       }
     }
   }
+}
+
+template <typename T, int NM, bool SP, bool WY, bool ST>
+MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
+                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
+                         const Params& p, int t0, int lane) {
+  if (nsteps == Stage<T, NM>::TT)
+    compute_tile_t<T, NM, SP, WY, ST, true>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
+  else
+    compute_tile_t<T, NM, SP, WY, ST, false>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
 }
 
 // Runs the recurrence over timesteps [t_begin, t_end) (t_begin tile-aligned), keeping kStages - 1
