@@ -221,207 +221,201 @@ MM_DEV void convert_bc(WarpSmem<T, NM>& sm, int slot, int lane) {
   }
 }
 
-// The recurrence runs in quarters of QS = 4 steps as a two-stage software pipeline per warp:
-//   P1 (MUFU-heavy): the per-step scalars of a quarter -- softplus(delta), exp(delta*A[0]) (or delta alone
-//       for a general A), delta*u, D*u, SiLU(z) -- independent across steps;
-//   P2 (FMA-heavy): the state update and the y contraction of a quarter, state pairs in the outer loop so
-//       that for a fixed pair the h update is the only dependency from one step to the next.
-// P1 of quarter q+1 is issued next to P2 of quarter q (crossing tile boundaries), so every warp's
-// instruction stream mixes both pipes instead of all warps of an SM alternating between MUFU-bound and
-// FMA-bound phases together.
-constexpr int QS = 4;
-
-struct Quarter {
-  float d[QS];   // ST: exp(delta*A[0]); general: delta * log2(e)
-  float du[QS];  // delta * u
-  float yd[QS];  // D * u
-  float g[QS];   // SiLU(z) (1 without z)
-  float dsum;    // sum of delta * log2(e) over the quarter's steps
-  float dmin;    // minimum of the same (raw delta only)
-};
-
-// P1 for steps [q*QS, q*QS + QS) of ring slot `slot` (nsteps: steps of the tile inside the range).
-template <typename T, int NM, bool SP, bool WY, bool ST>
-MM_DEV void phase1(const WarpSmem<T, NM>& sm, int slot, int q, int nsteps, float A0, float Dv, bool has_z, int lane,
-                   Quarter& o) {
+// Runs the recurrence over one half tile (HT steps, one 16-byte vector per row) at step offset kb of the
+// staged tile. WY: compute y. ST: A has the S4D-real structure.
+// Phase 1 computes every step's scalars (softplus(delta), exp(delta*A[0]), delta*u, D*u, SiLU(z)) --
+// independent across steps, so their MUFU latencies overlap. Phase 2 runs in sub-tiles of SK steps with
+// the state pairs in the outer loop: for a fixed pair the h update is the only dependency from one step
+// to the next; the decay powers, the B products and the y partial sums of the SK steps are independent.
+template <typename T, int NM, bool SP, bool WY, bool ST, bool FULL>
+MM_DEV void compute_half(const uint4& tu, const uint4& td, const uint4& tz, const float* __restrict__ sB,
+                         const float* __restrict__ sC, int kb, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
+                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, bool has_z,
+                         float (&yk)[Stage<T, NM>::HT]) {
   constexpr int HT = Stage<T, NM>::HT;
-  const int v = (q * QS) / HT;
-  const int e0 = (q * QS) % HT;
-  const uint4 tu = sm.io[slot][0][lane][v];
-  const uint4 td = sm.io[slot][1][lane][v];
-  uint4 tz = make_uint4(0, 0, 0, 0);
-  if (WY && has_z) tz = sm.io[slot][2][lane][v];
-  o.dsum = 0.f;
-  o.dmin = INFINITY;
+  constexpr int PS = Stage<T, NM>::PS;
+  float dk[HT];   // ST: exp(delta*A[0]); general: delta * log2(e)
+  float duk[HT];  // delta * u
+  float gk[HT];   // WY: SiLU(z) (1 without z)
 #pragma unroll
-  for (int kp = 0; kp < QS / 2; ++kp) {
-    const float2 xs = vec_pair<T>(tu, e0 / 2 + kp);
-    const float2 drs = vec_pair<T>(td, e0 / 2 + kp);
+  for (int kp = 0; kp < HT / 2; ++kp) {
+    const float2 xs = vec_pair<T>(tu, kp);
+    const float2 drs = vec_pair<T>(td, kp);
     float2 zs = make_float2(0.f, 0.f);
-    if (WY && has_z) zs = vec_pair<T>(tz, e0 / 2 + kp);
+    if (WY && has_z) zs = vec_pair<T>(tz, kp);
 #pragma unroll
     for (int s2 = 0; s2 < 2; ++s2) {
-      const int j = 2 * kp + s2;
+      const int k = 2 * kp + s2;
       const float x = s2 ? xs.y : xs.x;
       const float dr = s2 ? drs.y : drs.x;
       float d2 = SP ? softplus_log2(dr) : dr * kLog2e;
-      if (q * QS + j >= nsteps) d2 = 0.f;  // steps past the end: no decay, no input
-      o.dsum += d2;
-      if (!SP) o.dmin = fminf(o.dmin, d2);
-      o.d[j] = ST ? ex2(d2 * A0) : d2;
-      o.du[j] = d2 * x;
+      if (!FULL && k >= nsteps) d2 = 0.f;  // steps past the end: no decay, no input
+      sum_d2 += d2;
+      if (!SP) min_d2 = fminf(min_d2, d2);
+      dk[k] = ST ? ex2(d2 * A0) : d2;
+      duk[k] = d2 * x;
       if (WY) {
-        o.yd[j] = Dv * x;
-        o.g[j] = has_z ? silu(s2 ? zs.y : zs.x) : 1.0f;
+        yk[k] = Dv * x;
+        gk[k] = has_z ? silu(s2 ? zs.y : zs.x) : 1.0f;
+      }
+    }
+  }
+  constexpr int SK = HT < 4 ? HT : 4;
+#pragma unroll
+  for (int k0 = 0; k0 < HT; k0 += SK) {
+    f2_t a[SK], rr[SK], du2[SK], dd2[SK], y2[SK];
+#pragma unroll
+    for (int j = 0; j < SK; ++j) {
+      const int k = k0 + j;
+      du2[j] = f2_pack(duk[k], duk[k]);
+      y2[j] = f2_pack(0.f, 0.f);
+      if (ST) {
+        const float r = dk[k];
+        const float r2 = r * r;
+        a[j] = f2_pack(r, r2);
+        rr[j] = f2_pack(r2, r2);
+      } else {
+        dd2[j] = f2_pack(dk[k], dk[k]);
+      }
+    }
+#pragma unroll
+    for (int pi = 0; pi < NM / 2; ++pi) {
+      float4 bq[SK / 2], cq[SK / 2];
+#pragma unroll
+      for (int j2 = 0; j2 < SK / 2; ++j2) {
+        bq[j2] = *reinterpret_cast<const float4*>(sB + pi * PS + (kb + k0 + 2 * j2) * 2);
+        if (WY) cq[j2] = *reinterpret_cast<const float4*>(sC + pi * PS + (kb + k0 + 2 * j2) * 2);
+      }
+#pragma unroll
+      for (int j = 0; j < SK; ++j) {
+        if (FULL || k0 + j < nsteps) {
+          const float4& b4 = bq[j >> 1];
+          const f2_t bb = (j & 1) ? f2_pack(b4.z, b4.w) : f2_pack(b4.x, b4.y);
+          f2_t ap;
+          if (ST) {
+            if (pi > 0) a[j] = f2_mul(a[j], rr[j]);
+            ap = a[j];
+          } else {
+            const float2 arg = f2_unpack(f2_mul(dd2[j], A2[pi]));
+            ap = f2_pack(ex2(arg.x), ex2(arg.y));
+          }
+          h[pi] = f2_fma(ap, h[pi], f2_mul(du2[j], bb));
+          if (WY) {
+            const float4& c4 = cq[j >> 1];
+            y2[j] = f2_fma(h[pi], (j & 1) ? f2_pack(c4.z, c4.w) : f2_pack(c4.x, c4.y), y2[j]);
+          }
+        }
+      }
+    }
+    if (WY) {
+#pragma unroll
+      for (int j = 0; j < SK; ++j) {
+        const float2 ys = f2_unpack(y2[j]);
+        yk[k0 + j] = (yk[k0 + j] + (ys.x + ys.y)) * gk[k0 + j];
       }
     }
   }
 }
 
-// P2 for quarter q of the staged B/C tile; returns the quarter's outputs in y.
-template <typename T, int NM, bool WY, bool ST>
-MM_DEV void phase2(const float* __restrict__ sB, const float* __restrict__ sC, int q, int nsteps,
-                   const Quarter& S, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2], float (&y)[QS]) {
-  constexpr int PS = Stage<T, NM>::PS;
-  const int kb = q * QS;
-  f2_t a[QS], rr[QS], du2[QS], dd2[QS], y2[QS];
+// One staged tile = two half tiles. A full tile (the common case) is one branch-free block, so the
+// scheduler can overlap the second half's MUFU-heavy phase 1 with the first half's FMA-heavy phase 2.
+template <typename T, int NM, bool SP, bool WY, bool ST, bool FULLTILE>
+MM_DEV void compute_tile_t(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
+                           float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
+                           const Params& p, int t0, int lane) {
+  constexpr int HT = Stage<T, NM>::HT;
+  const float* sB = sm.bc;
+  const float* sC = sm.bc + Stage<T, NM>::COFF;
+  float yk[2][HT];
 #pragma unroll
-  for (int j = 0; j < QS; ++j) {
-    du2[j] = f2_pack(S.du[j], S.du[j]);
-    y2[j] = f2_pack(0.f, 0.f);
-    if (ST) {
-      const float r = S.d[j];
-      const float r2 = r * r;
-      a[j] = f2_pack(r, r2);
-      rr[j] = f2_pack(r2, r2);
-    } else {
-      dd2[j] = f2_pack(S.d[j], S.d[j]);
-    }
+  for (int v = 0; v < 2; ++v) {
+    const int ns = nsteps - v * HT;  // steps of this half inside the range
+    if (!FULLTILE && ns <= 0) break;
+    const uint4 tu = sm.io[slot][0][lane][v];
+    const uint4 td = sm.io[slot][1][lane][v];
+    uint4 tz = make_uint4(0, 0, 0, 0);
+    if (WY && p.has_z) tz = sm.io[slot][2][lane][v];
+    if (FULLTILE || ns >= HT)
+      compute_half<T, NM, SP, WY, ST, true>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, HT, sum_d2, min_d2, p.has_z,
+                                           yk[v]);
+    else
+      compute_half<T, NM, SP, WY, ST, false>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, ns, sum_d2, min_d2, p.has_z,
+                                            yk[v]);
   }
+  if (WY && ln.active) {
 #pragma unroll
-  for (int pi = 0; pi < NM / 2; ++pi) {
-    float4 bq[QS / 2], cq[QS / 2];
+    for (int v = 0; v < 2; ++v) {
+      const int ns = nsteps - v * HT;
+      if (!FULLTILE && ns <= 0) break;
+      const int tb = t0 + v * HT;
+      if ((FULLTILE || ns >= HT) && p.vec_io) {
+        uint4 yv;
 #pragma unroll
-    for (int j2 = 0; j2 < QS / 2; ++j2) {
-      bq[j2] = *reinterpret_cast<const float4*>(sB + pi * PS + (kb + 2 * j2) * 2);
-      if (WY) cq[j2] = *reinterpret_cast<const float4*>(sC + pi * PS + (kb + 2 * j2) * 2);
-    }
+        for (int kp = 0; kp < HT / 2; ++kp) vec_set_pair<T>(yv, kp, yk[v][2 * kp], yk[v][2 * kp + 1]);
+        __stcs(reinterpret_cast<uint4*>(ln.y_row + tb), yv);
+      } else {
 #pragma unroll
-    for (int j = 0; j < QS; ++j) {
-      if (kb + j < nsteps) {
-        const float4& b4 = bq[j >> 1];
-        const f2_t bb = (j & 1) ? f2_pack(b4.z, b4.w) : f2_pack(b4.x, b4.y);
-        f2_t ap;
-        if (ST) {
-          if (pi > 0) a[j] = f2_mul(a[j], rr[j]);
-          ap = a[j];
-        } else {
-          const float2 arg = f2_unpack(f2_mul(dd2[j], A2[pi]));
-          ap = f2_pack(ex2(arg.x), ex2(arg.y));
-        }
-        h[pi] = f2_fma(ap, h[pi], f2_mul(du2[j], bb));
-        if (WY) {
-          const float4& c4 = cq[j >> 1];
-          y2[j] = f2_fma(h[pi], (j & 1) ? f2_pack(c4.z, c4.w) : f2_pack(c4.x, c4.y), y2[j]);
-        }
+        for (int k = 0; k < HT; ++k)
+          if (k < ns) st_f32(ln.y_row + (long long)(tb + k) * p.ys[2], yk[v][k]);
       }
     }
   }
-  if (WY) {
-#pragma unroll
-    for (int j = 0; j < QS; ++j) {
-      const float2 ys = f2_unpack(y2[j]);
-      y[j] = (S.yd[j] + (ys.x + ys.y)) * S.g[j];
-    }
-  }
 }
 
-// Waits for ring slot `slot` (TMA: its barrier phase; cp.async: all outstanding groups) and makes the
-// tile visible to every lane.
-template <typename T, int NM>
-MM_DEV void wait_tile(WarpSmem<T, NM>& sm, int slot, unsigned& phases, const Params& p) {
-  if (p.use_tma) {
-    wait_tma_slot(&sm.bar[slot], phases, slot, p);
-  } else {
-    cp_async_wait<0>();
-    __syncwarp();
-  }
+template <typename T, int NM, bool SP, bool WY, bool ST>
+MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
+                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
+                         const Params& p, int t0, int lane) {
+  if (nsteps == Stage<T, NM>::TT)
+    compute_tile_t<T, NM, SP, WY, ST, true>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
+  else
+    compute_tile_t<T, NM, SP, WY, ST, false>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
 }
 
-// Runs the recurrence over timesteps [t_begin, t_end) (t_begin tile-aligned). Tiles pass through a
-// two-slot ring: tile i+1 is issued when tile i starts and awaited before tile i's last quarter (whose
-// P1 already reads it). With `stop_from` < t_end, the loop may end early at a tile boundary t >= stop_from
-// once every lane's slowest-decaying state has decayed below 2^kDecayCutoffLog2 over the range (the
-// recompute after a carry hand-off); returns the end reached. `phases` holds the parity of each TMA ring
-// slot's barrier and persists across calls.
+// Runs the recurrence over timesteps [t_begin, t_end) (t_begin tile-aligned), keeping kStages - 1
+// tiles of copies in flight ahead of the one being computed. With `stop_from` < t_end, the loop may end
+// early at a tile boundary t >= stop_from once every lane's slowest-decaying state has decayed below
+// 2^kDecayCutoffLog2 over the range (the recompute after a carry hand-off); returns the end reached.
+// `phases` holds the parity of each TMA ring slot's barrier and persists across calls.
 template <typename T, int NM, bool SP, bool WY, bool ST>
 MM_DEV int run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end, f2_t (&h)[NM / 2],
                      const f2_t (&A2)[NM / 2], float A0, float Dv, float& sum_d2, float& min_d2,
                      WarpSmem<T, NM>& sm, int lane, unsigned& phases, int stop_from = INT_MAX,
                      bool decays = false, float A_max = 0.f) {
   constexpr int TT = Stage<T, NM>::TT;
-  constexpr int HT = Stage<T, NM>::HT;
-  constexpr int NQ = TT / QS;  // quarters per tile
-  static_assert(kStages == 2, "the pipelined tile loop uses a two-slot ring");
   if (t_begin >= t_end) return t_end;
   const int ntiles = (t_end - t_begin + TT - 1) / TT;
   __syncwarp();  // earlier readers of the ring and of the B/C buffer are done
-  issue_tile<T, NM>(sm, 0, p, ln, t_begin, lane);
-  if (!p.use_tma) cp_async_commit();
-  wait_tile<T, NM>(sm, 0, phases, p);
-  Quarter S;
-  phase1<T, NM, SP, WY, ST>(sm, 0, 0, min(TT, t_end - t_begin), A0, Dv, p.has_z, lane, S);
+#pragma unroll
+  for (int i = 0; i < kStages - 1; ++i) {
+    if (i < ntiles) issue_tile<T, NM>(sm, i, p, ln, t_begin + i * TT, lane);
+    if (!p.use_tma) cp_async_commit();
+  }
   int t_done = t_end;
   for (int i = 0; i < ntiles; ++i) {
-    const int slot = i & 1;
-    const int t0 = t_begin + i * TT;
-    const int nsteps = min(TT, t_end - t0);
-    const bool more = i + 1 < ntiles;
-    if (more) {
-      issue_tile<T, NM>(sm, slot ^ 1, p, ln, t0 + TT, lane);
-      if (!p.use_tma) cp_async_commit();
+    const int nx = i + kStages - 1;
+    if (nx < ntiles) issue_tile<T, NM>(sm, nx % kStages, p, ln, t_begin + nx * TT, lane);
+    const int slot = i % kStages;
+    if (p.use_tma) {
+      wait_tma_slot(&sm.bar[slot], phases, slot, p);
+    } else {
+      cp_async_commit();
+      cp_async_wait<kStages - 1>();
     }
+    __syncwarp();
     convert_bc<T, NM>(sm, slot, lane);
     __syncwarp();
-    const float* sB = sm.bc;
-    const float* sC = sm.bc + Stage<T, NM>::COFF;
-    uint4 yv = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int q = 0; q < NQ; ++q) {
-      if (q * QS >= nsteps) break;
-      Quarter Sn;
-      const bool last_q = (q + 1) * QS >= nsteps;
-      if (!last_q) {
-        phase1<T, NM, SP, WY, ST>(sm, slot, q + 1, nsteps, A0, Dv, p.has_z, lane, Sn);
-      } else if (more) {
-        wait_tile<T, NM>(sm, slot ^ 1, phases, p);
-        phase1<T, NM, SP, WY, ST>(sm, slot ^ 1, 0, min(TT, t_end - t0 - TT), A0, Dv, p.has_z, lane, Sn);
-      }
-      float y[QS];
-      phase2<T, NM, WY, ST>(sB, sC, q, nsteps, S, h, A2, y);
-      sum_d2 += S.dsum;
-      if (!SP) min_d2 = fminf(min_d2, S.dmin);
-      if (WY && ln.active) {
-        const int e0 = (q * QS) % HT;  // position of this quarter inside its 16-byte output vector
-#pragma unroll
-        for (int j2 = 0; j2 < QS / 2; ++j2) vec_set_pair<T>(yv, e0 / 2 + j2, y[2 * j2], y[2 * j2 + 1]);
-        const bool vec_done = e0 + QS == HT;
-        const int tb = t0 + q * QS - e0;  // first step of the vector
-        if (p.vec_io && vec_done && tb + HT <= t0 + nsteps) {
-          __stcs(reinterpret_cast<uint4*>(ln.y_row + tb), yv);
-        } else if (!p.vec_io || tb + HT > t0 + nsteps) {
-#pragma unroll
-          for (int j = 0; j < QS; ++j)
-            if (q * QS + j < nsteps) st_f32(ln.y_row + (long long)(t0 + q * QS + j) * p.ys[2], y[j]);
-        }
-      }
-      S = Sn;
-    }
+    const int t0 = t_begin + i * TT;
+    compute_tile<T, NM, SP, WY, ST>(sm, slot, h, A2, A0, Dv, min(TT, t_end - t0), sum_d2, min_d2, ln, p, t0, lane);
     __syncwarp();  // B/C buffer and this slot are free for the next iteration
-    if (t0 + TT >= stop_from && more &&
+    if (t0 + TT >= stop_from && t0 + TT < t_end &&
         __all_sync(0xffffffffu, decays && (A_max * sum_d2 <= kDecayCutoffLog2))) {
       t_done = t0 + TT;
-      break;  // the next tile was already awaited (its P1 ran), so the ring stays in step
+      // drain the tiles already issued beyond this one so the ring's barrier phases stay in step
+      if (p.use_tma) {
+        for (int j = i + 1; j < min(i + kStages, ntiles); ++j) wait_tma_slot(&sm.bar[j % kStages], phases, j % kStages, p);
+      }
+      break;
     }
   }
   if (!p.use_tma) cp_async_wait<0>();
