@@ -73,7 +73,13 @@ struct Params {
   int silu;
 };
 
-// Channel-first (t contiguous). A warp covers 32 consecutive 8-element chunks of one (b, d) row.
+// Channel-first (t contiguous). A warp covers kCPT * 32 consecutive 8-element chunks of one (b, d) row:
+// lane l owns chunks l, l + 32, l + 64, ... so every load and store instruction of the warp is one
+// contiguous 512-byte (fp16) access, and all kCPT loads are in flight before the first is used. The
+// three-element causal halo of a chunk is the end of the previous chunk: the neighbouring lane's, lane 31's
+// previous chunk for lane 0, or memory for the warp's first chunk.
+constexpr int kCPT = 4;
+
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(256) conv_tfirst_kernel(const Params p, int chunks_per_row, int warps_per_row) {
   const int lane = threadIdx.x & 31;
@@ -81,58 +87,71 @@ __global__ void __launch_bounds__(256) conv_tfirst_kernel(const Params p, int ch
   const long long rows = (long long)p.batch * p.dim;
   if (gw >= rows * warps_per_row) return;
   const long long row = gw / warps_per_row;
-  const int chunk = (int)(gw % warps_per_row) * 32 + lane;
+  const int cbase = (int)(gw % warps_per_row) * 32 * kCPT;
   const int b = (int)(row / p.dim), d = (int)(row % p.dim);
   const T* xr = static_cast<const T*>(p.x) + b * p.xs[0] + d * p.xs[1];
   T* orow = static_cast<T*>(p.out) + b * p.os[0] + d * p.os[1];
-  const int t0 = chunk * kE;
-  float v[kE];
-  if (VEC && t0 + kE <= p.seqlen) {
-    load8<T>(xr + t0, v);
-  } else {
+  float v[kCPT][kE];
 #pragma unroll
-    for (int k = 0; k < kE; ++k) v[k] = (t0 + k < p.seqlen) ? ld_f32(xr + (long long)(t0 + k) * p.xs[2]) : 0.f;
+  for (int j = 0; j < kCPT; ++j) {
+    const int t0 = (cbase + j * 32 + lane) * kE;
+    if (VEC && t0 + kE <= p.seqlen) {
+      load8<T>(xr + t0, v[j]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < kE; ++k) v[j][k] = (t0 + k < p.seqlen) ? ld_f32(xr + (long long)(t0 + k) * p.xs[2]) : 0.f;
+    }
   }
-  // halo x[t0-3 .. t0-1]: from the previous lane, or from memory for lane 0
-  float h0 = __shfl_up_sync(0xffffffffu, v[5], 1);
-  float h1 = __shfl_up_sync(0xffffffffu, v[6], 1);
-  float h2 = __shfl_up_sync(0xffffffffu, v[7], 1);
-  if (lane == 0) {
-    h0 = t0 - 3 >= 0 ? ld_f32(xr + (long long)(t0 - 3) * p.xs[2]) : 0.f;
-    h1 = t0 - 2 >= 0 ? ld_f32(xr + (long long)(t0 - 2) * p.xs[2]) : 0.f;
-    h2 = t0 - 1 >= 0 ? ld_f32(xr + (long long)(t0 - 1) * p.xs[2]) : 0.f;
-  }
-  if (chunk >= chunks_per_row) return;
   const float w0 = p.w[d * kW + 0], w1 = p.w[d * kW + 1], w2 = p.w[d * kW + 2], w3 = p.w[d * kW + 3];
   const float bb = p.bias ? p.bias[d] : 0.f;
-  float win[kE + 3] = {h0, h1, h2};
 #pragma unroll
-  for (int k = 0; k < kE; ++k) win[k + 3] = v[k];
-  float o[kE];
+  for (int j = 0; j < kCPT; ++j) {
+    const int chunk = cbase + j * 32 + lane;
+    const int t0 = chunk * kE;
+    // halo x[t0-3 .. t0-1]
+    float h0 = __shfl_up_sync(0xffffffffu, v[j][5], 1);
+    float h1 = __shfl_up_sync(0xffffffffu, v[j][6], 1);
+    float h2 = __shfl_up_sync(0xffffffffu, v[j][7], 1);
+    if (j > 0) {
+      const float p0 = __shfl_sync(0xffffffffu, v[j - 1][5], 31);
+      const float p1 = __shfl_sync(0xffffffffu, v[j - 1][6], 31);
+      const float p2 = __shfl_sync(0xffffffffu, v[j - 1][7], 31);
+      if (lane == 0) { h0 = p0; h1 = p1; h2 = p2; }
+    } else if (lane == 0) {
+      h0 = t0 - 3 >= 0 ? ld_f32(xr + (long long)(t0 - 3) * p.xs[2]) : 0.f;
+      h1 = t0 - 2 >= 0 ? ld_f32(xr + (long long)(t0 - 2) * p.xs[2]) : 0.f;
+      h2 = t0 - 1 >= 0 ? ld_f32(xr + (long long)(t0 - 1) * p.xs[2]) : 0.f;
+    }
+    if (chunk >= chunks_per_row) continue;
+    float win[kE + 3] = {h0, h1, h2};
 #pragma unroll
-  for (int k = 0; k < kE; ++k) {
-    float s = bb;
-    s = fmaf(w0, win[k], s);
-    s = fmaf(w1, win[k + 1], s);
-    s = fmaf(w2, win[k + 2], s);
-    s = fmaf(w3, win[k + 3], s);
-    o[k] = act(s, p.silu);
-  }
-  if (VEC && t0 + kE <= p.seqlen) {
-    store8<T>(orow + t0, o);
-  } else {
+    for (int k = 0; k < kE; ++k) win[k + 3] = v[j][k];
+    float o[kE];
 #pragma unroll
-    for (int k = 0; k < kE; ++k)
-      if (t0 + k < p.seqlen) st_f32(orow + (long long)(t0 + k) * p.os[2], o[k]);
-  }
-  // conv-state hand-off: the last kW inputs of the row, taken by the chunk that holds t = seqlen - 1
-  if (p.conv_state && t0 <= p.seqlen - 1 && p.seqlen - 1 < t0 + kE) {
-    const int last = p.seqlen - 1 - t0;  // index of t = seqlen-1 in v
-    float* cs = p.conv_state + ((long long)b * p.dim + d) * kW;
+    for (int k = 0; k < kE; ++k) {
+      float sacc = bb;
+      sacc = fmaf(w0, win[k], sacc);
+      sacc = fmaf(w1, win[k + 1], sacc);
+      sacc = fmaf(w2, win[k + 2], sacc);
+      sacc = fmaf(w3, win[k + 3], sacc);
+      o[k] = act(sacc, p.silu);
+    }
+    if (VEC && t0 + kE <= p.seqlen) {
+      store8<T>(orow + t0, o);
+    } else {
 #pragma unroll
-    for (int k = 0; k < kW; ++k) {
-      const int t = p.seqlen - kW + k;
-      cs[k] = t >= 0 ? win[last + 3 - (kW - 1) + k] : 0.f;
+      for (int k = 0; k < kE; ++k)
+        if (t0 + k < p.seqlen) st_f32(orow + (long long)(t0 + k) * p.os[2], o[k]);
+    }
+    // conv-state hand-off: the last kW inputs of the row, taken by the chunk that holds t = seqlen - 1
+    if (p.conv_state && t0 <= p.seqlen - 1 && p.seqlen - 1 < t0 + kE) {
+      const int last = p.seqlen - 1 - t0;  // index of t = seqlen-1 in this chunk
+      float* cs = p.conv_state + ((long long)b * p.dim + d) * kW;
+#pragma unroll
+      for (int k = 0; k < kW; ++k) {
+        const int t = p.seqlen - kW + k;
+        cs[k] = t >= 0 ? win[last + k] : 0.f;
+      }
     }
   }
 }
@@ -180,6 +199,7 @@ __global__ void __launch_bounds__(256) conv_dlast_kernel(const Params p, int run
   load_row(t_begin - 3, x0);
   load_row(t_begin - 2, x1);
   load_row(t_begin - 1, x2);
+#pragma unroll 4
   for (int t = t_begin; t < t_end; ++t) {
     load_row(t, x3);
     float o[kE];
@@ -261,7 +281,7 @@ static cudaError_t launch_fwd(const Params& p, cudaStream_t s) {
     const bool vec = aligned16(p.x) && aligned16(p.out) && p.xs[0] % epv == 0 && p.xs[1] % epv == 0 &&
                      p.os[0] % epv == 0 && p.os[1] % epv == 0;
     const int cpr = (p.seqlen + kE - 1) / kE;
-    const int wpr = (cpr + 31) / 32;
+    const int wpr = (cpr + 32 * kCPT - 1) / (32 * kCPT);
     const long long warps = (long long)p.batch * p.dim * wpr;
     const long long blocks = (warps + 7) / 8;
     if (vec) conv_tfirst_kernel<T, true><<<(unsigned)blocks, 256, 0, s>>>(p, cpr, wpr);
