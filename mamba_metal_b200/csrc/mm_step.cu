@@ -84,35 +84,67 @@ struct NormParams {
   float eps;
 };
 
-// One CTA per row; the row is kept in registers between the sum-of-squares and the scaling pass.
-template <typename T, int PER>
-__global__ void __launch_bounds__(256) add_rmsnorm_kernel(const NormParams p) {
+// One CTA per row, ceil(dim / 8) threads, 8 consecutive elements per thread: the residual (fp32, two
+// 16-byte loads) and the delta (one 16-byte load for 16-bit types) are all in flight before the single
+// block reduction; the row stays in registers for the scaling pass.
+constexpr int kNormE = 8;
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(1024) add_rmsnorm_kernel(const NormParams p) {
   const int r = blockIdx.x;
   float* res = p.res + (long long)r * p.dim;
   const T* dl = p.delta ? static_cast<const T*>(p.delta) + (long long)r * p.dsr : nullptr;
-  float v[PER];
+  const int c0 = threadIdx.x * kNormE;
+  float v[kNormE];
+  if (VEC && c0 + kNormE <= p.dim) {
+    const float4 a = *reinterpret_cast<const float4*>(res + c0);
+    const float4 b = *reinterpret_cast<const float4*>(res + c0 + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    if (dl) {
+      float d8[kNormE];
+      if (sizeof(T) == 2) {
+        const uint4 q = *reinterpret_cast<const uint4*>(dl + c0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 e = vec_pair<T>(q, k);
+          d8[2 * k] = e.x;
+          d8[2 * k + 1] = e.y;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < kNormE; ++k) d8[k] = ld_f32(dl + c0 + k);
+      }
+#pragma unroll
+      for (int k = 0; k < kNormE; ++k) v[k] += d8[k];
+      *reinterpret_cast<float4*>(res + c0) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(res + c0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kNormE; ++k) {
+      const int c = c0 + k;
+      float x = 0.f;
+      if (c < p.dim) {
+        x = res[c];
+        if (dl) {
+          x += ld_f32(dl + c);
+          res[c] = x;
+        }
+      }
+      v[k] = x;
+    }
+  }
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    const int c = threadIdx.x + i * blockDim.x;
-    float x = 0.f;
-    if (c < p.dim) {
-      x = res[c];
-      if (dl) {
-        x += ld_f32(dl + c);
-        res[c] = x;
-      }
-    }
-    v[i] = x;
-    ss = fmaf(x, x, ss);
-  }
+  for (int k = 0; k < kNormE; ++k) ss = fmaf(v[k], v[k], ss);
   __shared__ float red[32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const int nw = (blockDim.x + 31) >> 5;
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    float t = threadIdx.x < nw ? red[threadIdx.x] : 0.f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
     if (threadIdx.x == 0) red[0] = t;
@@ -120,22 +152,34 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const NormParams p) {
   __syncthreads();
   const float inv = rsqrtf(red[0] / (float)p.dim + p.eps);
   T* out = static_cast<T*>(p.out) + (long long)r * p.osr;
+  if (VEC && c0 + kNormE <= p.dim) {
+    const float4 wa = *reinterpret_cast<const float4*>(p.w + c0);
+    const float4 wb = *reinterpret_cast<const float4*>(p.w + c0 + 4);
+    const float w8[kNormE] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    if (sizeof(T) == 2) {
+      uint4 q;
 #pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    const int c = threadIdx.x + i * blockDim.x;
-    if (c < p.dim) st_f32(out + c, v[i] * inv * p.w[c]);
+      for (int k = 0; k < 4; ++k) vec_set_pair<T>(q, k, v[2 * k] * inv * w8[2 * k], v[2 * k + 1] * inv * w8[2 * k + 1]);
+      *reinterpret_cast<uint4*>(out + c0) = q;
+    } else {
+#pragma unroll
+      for (int k = 0; k < kNormE; ++k) st_f32(out + c0 + k, v[k] * inv * w8[k]);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kNormE; ++k) {
+      const int c = c0 + k;
+      if (c < p.dim) st_f32(out + c, v[k] * inv * p.w[c]);
+    }
   }
 }
 
 template <typename T>
-static cudaError_t launch_norm(const NormParams& p, cudaStream_t s) {
-  const int per = (p.dim + 255) / 256;
-  if (per <= 2) add_rmsnorm_kernel<T, 2><<<p.rows, 256, 0, s>>>(p);
-  else if (per <= 4) add_rmsnorm_kernel<T, 4><<<p.rows, 256, 0, s>>>(p);
-  else if (per <= 8) add_rmsnorm_kernel<T, 8><<<p.rows, 256, 0, s>>>(p);
-  else if (per <= 16) add_rmsnorm_kernel<T, 16><<<p.rows, 256, 0, s>>>(p);
-  else if (per <= 32) add_rmsnorm_kernel<T, 32><<<p.rows, 256, 0, s>>>(p);
-  else return cudaErrorInvalidValue;
+static cudaError_t launch_norm(const NormParams& p, bool vec, cudaStream_t s) {
+  const int threads = ((p.dim + kNormE - 1) / kNormE + 31) / 32 * 32;
+  if (threads > 1024) return cudaErrorInvalidValue;
+  if (vec) add_rmsnorm_kernel<T, true><<<p.rows, threads, 0, s>>>(p);
+  else add_rmsnorm_kernel<T, false><<<p.rows, threads, 0, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -170,7 +214,7 @@ extern "C" int mm_ssm_decode_step(const MMSSMStepArgs* a, mm_stream_t stream) {
 extern "C" int mm_add_rmsnorm(const MMAddNormArgs* a, mm_stream_t stream) {
   if (!a) return MM_ERR_ARG;
   if (dtype_size(a->dtype) == 0) return MM_ERR_DTYPE;
-  if (a->rows < 0 || a->dim < 1 || a->dim > 32 * 256) return MM_ERR_SHAPE;
+  if (a->rows < 0 || a->dim < 1 || a->dim > 1024 * 8) return MM_ERR_SHAPE;
   if (a->rows > (1LL << 31) - 1) return MM_ERR_SHAPE;
   if (a->rows == 0) return MM_OK;
   if (!a->residual || !a->weight || !a->out) return MM_ERR_ARG;
@@ -179,10 +223,13 @@ extern "C" int mm_add_rmsnorm(const MMAddNormArgs* a, mm_stream_t stream) {
   p.dsr = a->delta_stride_r; p.osr = a->out_stride_r; p.rows = (int)a->rows; p.dim = (int)a->dim;
   p.eps = (float)a->eps;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // 16-byte vectors when every row start is aligned (dim, row strides multiples of 8 elements)
+  const bool vec = a->dim % 8 == 0 && aligned16(a->residual) && aligned16(a->weight) && aligned16(a->out) &&
+                   a->out_stride_r % 8 == 0 && (!a->delta || (aligned16(a->delta) && a->delta_stride_r % 8 == 0));
   cudaError_t e;
-  if (a->dtype == MM_F32) e = step::launch_norm<float>(p, s);
-  else if (a->dtype == MM_F16) e = step::launch_norm<__half>(p, s);
-  else e = step::launch_norm<__nv_bfloat16>(p, s);
+  if (a->dtype == MM_F32) e = step::launch_norm<float>(p, vec, s);
+  else if (a->dtype == MM_F16) e = step::launch_norm<__half>(p, vec, s);
+  else e = step::launch_norm<__nv_bfloat16>(p, vec, s);
   return e == cudaSuccess ? MM_OK : MM_ERR_LAUNCH;
 }
 
