@@ -399,7 +399,7 @@ def run_decode(args, rank, world, local_rank):
     with torch.no_grad():
         model = init_weights_(MambaModel(cfg, dtype=torch.bfloat16, device=dev), seed=0)
         if world > 1:
-            model = tp_model(model, rank, world)
+            model = tp_model(model, rank, world, peer_rows=c["batch"])
             torch.cuda.empty_cache()
     ids_host = torch.randint(0, c["vocab_size"], (c["batch"], c["prompt"]),
                              generator=torch.Generator().manual_seed(0)).pin_memory()
@@ -449,8 +449,10 @@ def run_decode(args, rank, world, local_rank):
         "e2e": {"value": c["batch"] * n_new / (e2e_ms * 1e-3), "unit": "tok/s", "ms": e2e_ms,
                 "h2d_bytes_per_step": ids_host.numel() * 8 / n_new, "d2h_bytes_per_step": c["batch"] * 8,
                 "note": "prompt H2D + prefill + 256 greedy steps + ids D2H, per generated token"},
-        # libmamba_b200 kernels per step: conv step, SSM step and residual-norm per layer, plus the first norm
-        "gpu_launches": args.steps * (3 * c["n_layer"] + 1), "clocks": clk.summary()}), flush=True)
+        # libmamba_b200 kernels per step: conv step, SSM step and residual-norm per layer (+ two peer
+        # all-reduces per layer under tensor parallelism), plus the first norm
+        "gpu_launches": args.steps * ((3 + (2 if world > 1 else 0)) * c["n_layer"] + 1), "clocks": clk.summary()}),
+          flush=True)
 
 
 def main():

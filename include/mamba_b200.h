@@ -222,6 +222,28 @@ typedef struct MMAddNormArgs {
 
 int mm_add_rmsnorm(const MMAddNormArgs* args, mm_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * One-shot all-reduce over peer memory, for the tensor-parallel decode step (a B200 addition: the
+ * reference has no multi-device code). Each rank has written its n-element partial into its own
+ * 16-byte aligned slot; bufs[r] / signals[r] are rank r's slot and signal pad as mapped in this process
+ * (symmetric memory). CTA c signals slice c ready to every peer (epoch from counters[c]), waits at most
+ * 2 s for every peer, then sums slice c of all slots with plain peer loads (fp32 accumulation) into the
+ * local `out`. The signal pads need nblocks * MM_MAX_TP words, zero-initialised; counters: nblocks + 1
+ * words of local device memory, zero-initialised (the last one is an error flag set on a wait timeout).
+ * All ranks must make the same sequence of calls with the same nblocks.
+ * ------------------------------------------------------------------------------------------- */
+#define MM_MAX_TP 8
+#define MM_PEER_MAX_BLOCKS 64
+typedef struct MMPeerReduceArgs {
+  const void* bufs[MM_MAX_TP];
+  unsigned* signals[MM_MAX_TP];
+  unsigned* counters;
+  void* out;
+  int64_t dtype, n, world, rank, nblocks;
+} MMPeerReduceArgs;
+
+int mm_peer_allreduce(const MMPeerReduceArgs* args, mm_stream_t stream);
+
 /* Library version string (static storage). */
 const char* mm_version(void);
 

@@ -72,6 +72,17 @@ class MMAddNormArgs(ctypes.Structure):
     ]
 
 
+MM_MAX_TP = 8
+MM_PEER_MAX_BLOCKS = 64
+
+
+class MMPeerReduceArgs(ctypes.Structure):
+    _fields_ = [
+        ("bufs", _p * MM_MAX_TP), ("signals", _p * MM_MAX_TP), ("counters", _p), ("out", _p),
+        ("dtype", _i64), ("n", _i64), ("world", _i64), ("rank", _i64), ("nblocks", _i64),
+    ]
+
+
 _SIGNATURES = {
     "mm_selective_scan_workspace_size": ([ctypes.POINTER(MMScanArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "mm_selective_scan_fwd": ([ctypes.POINTER(MMScanArgs), _p, ctypes.c_size_t, _p], ctypes.c_int),
@@ -82,6 +93,7 @@ _SIGNATURES = {
     "mm_causal_conv1d_step": ([ctypes.POINTER(MMConvStepArgs), _p], ctypes.c_int),
     "mm_ssm_decode_step": ([ctypes.POINTER(MMSSMStepArgs), _p], ctypes.c_int),
     "mm_add_rmsnorm": ([ctypes.POINTER(MMAddNormArgs), _p], ctypes.c_int),
+    "mm_peer_allreduce": ([ctypes.POINTER(MMPeerReduceArgs), _p], ctypes.c_int),
     "mm_version": ([], ctypes.c_char_p),
 }
 

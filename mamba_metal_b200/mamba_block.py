@@ -40,6 +40,7 @@ class MambaBlock(nn.Module):
         # with tensor parallelism (mamba_metal_b200.parallel) this block holds 1/tp_world of the channels
         self.d_inner = expand * d_model // tp_world
         self.tp_reduce = None  # set by mamba_metal_b200.parallel.tp_model: sums row-parallel partials
+        self.tp_sites = (0, 1)  # this block's call sites (x_proj, out_proj) in the peer all-reduce
         self.dt_rank = math.ceil(d_model / 16) if dt_rank is None else dt_rank
         kw = dict(dtype=dtype, device=device)
         self.in_proj = nn.Linear(d_model, self.d_inner * 2, bias=False, **kw)
@@ -53,11 +54,12 @@ class MambaBlock(nn.Module):
         self.out_proj = nn.Linear(self.d_inner, d_model, bias=False, **kw)
         self._A_cache = None
 
-    def _project(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    def _project(self, x: torch.Tensor, w: torch.Tensor, site: int) -> torch.Tensor:
         """x @ w.T; for a tensor-parallel block (x_proj, out_proj are row-parallel) the partial products
-        are all-reduced over the group."""
-        y = F.linear(x, w)
-        return self.tp_reduce(y) if self.tp_reduce is not None else y
+        are all-reduced over the group (site 0: x_proj, 1: out_proj)."""
+        if self.tp_reduce is None:
+            return F.linear(x, w)
+        return self.tp_reduce(x, w, self.tp_sites[site])
 
     # A = -exp(A_log) (mamba_block.py:87, :138), cached until A_log changes
     def _A(self) -> torch.Tensor:
@@ -77,7 +79,7 @@ class MambaBlock(nn.Module):
         conv_state = torch.empty((bsz, E, self.d_conv), dtype=torch.float32, device=x.device) if want_state else None
         ops.causal_conv1d(x_in, self.conv1d.weight, self.conv1d.bias, silu=True, out=xc.transpose(1, 2),
                           conv_state_out=conv_state)
-        x_dbl = self._project(xc, self.x_proj.weight)                    # (B, L, R + 2N)
+        x_dbl = self._project(xc, self.x_proj.weight, 0)                    # (B, L, R + 2N)
         dt = F.linear(x_dbl[..., :R], self.dt_proj.weight, self.dt_proj.bias)  # (B, L, E), bias included
         Bm = x_dbl[..., R:R + N].transpose(1, 2)                         # (B, N, L) view
         Cm = x_dbl[..., R + N:].transpose(1, 2)
@@ -86,7 +88,7 @@ class MambaBlock(nn.Module):
         Df = self.D if self.D.dtype == torch.float32 else self.D.float()
         selective_scan_into(xc.transpose(1, 2), dt.transpose(1, 2), self._A(), Bm, Cm, Df, z,
                             y.transpose(1, 2), ssm_state, delta_softplus=True)
-        out = self._project(y, self.out_proj.weight)
+        out = self._project(y, self.out_proj.weight, 1)
         return out, conv_state, ssm_state
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -109,9 +111,9 @@ class MambaBlock(nn.Module):
             ssm_state = ssm_state.to(torch.float32, copy=True).contiguous()
         xz = F.linear(x_token[:, 0].to(dt_), self.in_proj.weight)       # (B, 2E)
         xc = ops.causal_conv1d_step(xz[:, :E], conv_state, self.conv1d.weight, self.conv1d.bias, silu=True)
-        x_dbl = self._project(xc, self.x_proj.weight)                    # (B, R + 2N)
+        x_dbl = self._project(xc, self.x_proj.weight, 0)                    # (B, R + 2N)
         dt = F.linear(x_dbl[:, :R], self.dt_proj.weight, self.dt_proj.bias)
         Df = self.D if self.D.dtype == torch.float32 else self.D.float()
         y = ops.ssm_decode_step(xc, dt, xz[:, E:], x_dbl[:, R:R + N], x_dbl[:, R + N:], self._A(), Df, ssm_state,
                                 dt_softplus=True)
-        return self._project(y, self.out_proj.weight)[:, None, :], conv_state, ssm_state
+        return self._project(y, self.out_proj.weight, 1)[:, None, :], conv_state, ssm_state

@@ -18,6 +18,8 @@ from __future__ import annotations
 
 import torch
 import torch.distributed as dist
+import torch.nn.functional as F
+
 from mamba_metal_b200.mamba_model import MambaConfig, MambaModel
 
 
@@ -50,28 +52,38 @@ def shard_state_dict(sd: dict, cfg: MambaConfig, rank: int, world: int) -> dict:
     return {k: v.contiguous() for k, v in out.items()}
 
 
-class _AllReduce:
-    """Sums a partial projection output over the tensor-parallel group, in float32."""
+class _TPProject:
+    """Row-parallel projection + all-reduce. Decode-sized partials (at most `max_rows` rows) are written
+    straight into their call site's peer-memory slot and summed by the library's peer all-reduce
+    kernel; larger ones (prefill) are reduced by NCCL in float32."""
 
-    def __init__(self, group):
+    def __init__(self, group, peer=None, max_rows: int = 0):
         self.group = group
+        self.peer = peer
+        self.max_rows = max_rows
 
-    def __call__(self, t: torch.Tensor) -> torch.Tensor:
-        if t.dtype == torch.float32:
-            t = t.contiguous()
-            dist.all_reduce(t, group=self.group)
-            return t
-        t32 = t.float()
+    def __call__(self, x: torch.Tensor, w: torch.Tensor, site: int) -> torch.Tensor:
+        rows = x.numel() // x.shape[-1]
+        n = rows * w.shape[0]
+        peer = self.peer
+        if peer is not None and rows <= self.max_rows and x.dtype == peer.dtype and n <= peer.capacity[site]:
+            part = peer.slot(site)[:n].view(rows, w.shape[0])
+            torch.matmul(x.reshape(rows, x.shape[-1]), w.t(), out=part)
+            out = torch.empty((rows, w.shape[0]), dtype=x.dtype, device=x.device)
+            peer.reduce(site, n, out)
+            return out.view(*x.shape[:-1], w.shape[0])
+        t32 = F.linear(x, w).float()
         dist.all_reduce(t32, group=self.group)
-        return t32.to(t.dtype)
+        return t32.to(x.dtype)
 
 
-def tp_model(full: MambaModel, rank: int, world: int, group=None) -> MambaModel:
+def tp_model(full: MambaModel, rank: int, world: int, group=None, peer_rows: int = 0) -> MambaModel:
     """Builds this rank's tensor-parallel MambaModel from a full one (same device and dtype).
 
     The returned model holds the local channel slice in every mixer and all-reduces after x_proj and
     after out_proj; its forward / prefill / step / generation API is unchanged (conv and SSM states
-    are per-rank slices of d_inner)."""
+    are per-rank slices of d_inner). With peer_rows > 0, projections of up to that many rows (decode
+    batches) reduce through NVLink peer memory instead of NCCL."""
     cfg = full.cfg
     dev = full.embeddings.weight.device
     sd = shard_state_dict(full.state_dict(), cfg, rank, world)
@@ -79,7 +91,18 @@ def tp_model(full: MambaModel, rank: int, world: int, group=None) -> MambaModel:
         local = MambaModel(cfg, dtype=full.dtype, tp_world=world)
     local = local.to_empty(device=dev)
     local.load_state_dict(sd, strict=True)
-    reduce = _AllReduce(group)
-    for layer in local.layers:
-        layer.mixer.tp_reduce = reduce
+    peer = None
+    if peer_rows > 0 and world > 1:
+        from mamba_metal_b200.comm import PeerAllReduce
+
+        dt_rank = local.layers[0].mixer.dt_rank
+        sites = []
+        for _ in local.layers:
+            sites += [peer_rows * (dt_rank + 2 * cfg.d_state), peer_rows * cfg.d_model]
+        peer = PeerAllReduce(group if group is not None else dist.group.WORLD, dev, full.dtype, sites)
+    proj = _TPProject(group, peer, peer_rows)
+    for i, layer in enumerate(local.layers):
+        layer.mixer.tp_reduce = proj
+        layer.mixer.tp_sites = (2 * i, 2 * i + 1)
+    local.tp_peer = peer
     return local

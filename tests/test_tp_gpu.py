@@ -16,7 +16,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, peer_rows=0):
     import datetime
 
     import torch.distributed as dist
@@ -38,7 +38,7 @@ def _worker(rank, world, port, q):
             ref_logits = full(ids)
             _, ref_conv, ref_ssm = full.prefill(ids)
             ref_out = generate_ids(full, ids, 8)
-            tp = tp_model(full, rank, world)
+            tp = tp_model(full, rank, world, peer_rows=peer_rows)
             logits = tp(ids)
             _, conv, ssm = tp.prefill(ids)
             out = generate_ids(tp, ids, 8)
@@ -47,6 +47,8 @@ def _worker(rank, world, port, q):
         ok_state = torch.allclose(ssm[1], ref_ssm[1][:, lo:lo + tp.d_inner], rtol=1e-4, atol=1e-5)
         ok_conv = torch.allclose(conv[2], ref_conv[2][:, lo:lo + tp.d_inner], rtol=1e-5, atol=1e-6)
         same_tokens = bool(torch.equal(out, ref_out))
+        if tp.tp_peer is not None:
+            assert not tp.tp_peer.timed_out()
         q.put((rank, ok_logits, ok_state, ok_conv, same_tokens, float((logits - ref_logits).abs().max())))
     except Exception as e:  # pragma: no cover - reported to the parent
         q.put((rank, False, False, False, False, repr(e)))
@@ -55,13 +57,15 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_single_gpu():
+@pytest.mark.parametrize("peer_rows", [0, 64])
+def test_tp2_matches_single_gpu(peer_rows):
+    """NCCL reductions (peer_rows=0) and the NVLink peer all-reduce for decode-sized projections."""
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, peer_rows)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(2)]
