@@ -224,22 +224,33 @@ int mm_add_rmsnorm(const MMAddNormArgs* args, mm_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------
  * One-shot all-reduce over peer memory, for the tensor-parallel decode step (a B200 addition: the
- * reference has no multi-device code). Each rank has written its n-element partial into its own
- * 16-byte aligned slot; bufs[r] / signals[r] are rank r's slot and signal pad as mapped in this process
- * (symmetric memory). CTA c signals slice c ready to every peer (epoch from counters[c]), waits at most
- * 2 s for every peer, then sums slice c of all slots with plain peer loads (fp32 accumulation) into the
- * local `out`. The signal pads need nblocks * MM_MAX_TP words, zero-initialised; counters: nblocks + 1
- * words of local device memory, zero-initialised (the last one is an error flag set on a wait timeout).
- * All ranks must make the same sequence of calls with the same nblocks.
+ * reference has no multi-device code). Every rank owns a receive area of `world` regions, `stride`
+ * elements apart, in memory that all ranks map (symmetric memory); slots[r] is rank r's area as mapped
+ * in this process. Before the call each rank has written its n-element partial at the start of region
+ * `rank` of its own area. Two protocols:
+ *   MM_PEER_FLAGS: CTA c stores slice c of the partial into region `rank` of every peer's area (posted
+ *     NVLink stores), then tells each peer "slice c of call e has arrived" through the signal pads
+ *     (epoch e from counters[c]); it waits for every peer's word, then sums slice c of the `world`
+ *     partials from local memory into `out`. Signal pads: MM_PEER_MAX_BLOCKS * MM_MAX_TP words each.
+ *   MM_PEER_LL (low latency, small n): the partial travels as 16-byte lines of two data words, each
+ *     beside the call's epoch in the same 8-byte half; receivers poll the lines themselves (no fence,
+ *     no signal pad). Needs stride * element size >= 2 * (n * element size rounded up to 8 bytes).
+ * Sums are in fp32 in rank order; every wait gives up after 2 s and sets the error word. counters:
+ * MM_PEER_MAX_BLOCKS + 3 words of local device memory, zero-initialised (flag epochs, the error word,
+ * the LL epoch and a ticket); areas and pads zero-initialised. All ranks must make the same sequence of
+ * calls with the same n, protocol and nblocks; peers rewrite an area as soon as they have passed the
+ * previous call, so consecutive calls must use different areas.
  * ------------------------------------------------------------------------------------------- */
 #define MM_MAX_TP 8
 #define MM_PEER_MAX_BLOCKS 64
+#define MM_PEER_FLAGS 0
+#define MM_PEER_LL 1
 typedef struct MMPeerReduceArgs {
-  const void* bufs[MM_MAX_TP];
+  void* slots[MM_MAX_TP];
   unsigned* signals[MM_MAX_TP];
   unsigned* counters;
   void* out;
-  int64_t dtype, n, world, rank, nblocks;
+  int64_t dtype, n, stride, world, rank, nblocks, protocol;
 } MMPeerReduceArgs;
 
 int mm_peer_allreduce(const MMPeerReduceArgs* args, mm_stream_t stream);

@@ -74,12 +74,14 @@ class MMAddNormArgs(ctypes.Structure):
 
 MM_MAX_TP = 8
 MM_PEER_MAX_BLOCKS = 64
+MM_PEER_FLAGS, MM_PEER_LL = 0, 1
 
 
 class MMPeerReduceArgs(ctypes.Structure):
     _fields_ = [
-        ("bufs", _p * MM_MAX_TP), ("signals", _p * MM_MAX_TP), ("counters", _p), ("out", _p),
-        ("dtype", _i64), ("n", _i64), ("world", _i64), ("rank", _i64), ("nblocks", _i64),
+        ("slots", _p * MM_MAX_TP), ("signals", _p * MM_MAX_TP), ("counters", _p), ("out", _p),
+        ("dtype", _i64), ("n", _i64), ("stride", _i64), ("world", _i64), ("rank", _i64), ("nblocks", _i64),
+        ("protocol", _i64),
     ]
 
 

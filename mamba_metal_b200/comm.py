@@ -18,15 +18,17 @@ from mamba_metal_b200 import _lib
 class PeerAllReduce:
     """All-reduce of small partial sums through NVLink peer memory.
 
-    ``slot_numels[i]`` is the largest partial (in elements) call site i will reduce. Each site gets its
-    own slot in one symmetric buffer; a producer writes its partial straight into ``slot(i)`` (e.g. as a
-    GEMM output) and ``reduce(i, n, out)`` sums the n-element partials of every rank into ``out``.
-    Sites reuse their slot only on their next call, and the kernel's barrier keeps ranks at most one call
-    apart, so no slot is overwritten while a peer still reads it. All ranks must make the same sequence
+    ``slot_numels[i]`` is the largest partial (in elements) call site i will reduce. Each site owns a
+    receive area of ``world`` partials in one symmetric buffer; a producer writes this rank's partial
+    straight into ``slot(i)`` (e.g. as a GEMM output) and ``reduce(i, n, out)`` sums the n-element
+    partials of every rank into ``out``. Peers rewrite a site's area as soon as they have passed the
+    previous call, so consecutive calls must use different sites; all ranks must make the same sequence
     of calls.
     """
 
-    def __init__(self, group, device, dtype: torch.dtype, slot_numels: list[int], nblocks: int = 16):
+    THREADS = 256  # the kernel's CTA size
+
+    def __init__(self, group, device, dtype: torch.dtype, slot_numels: list[int], ll_max_bytes: int = 1 << 20):
         import torch.distributed._symmetric_memory as symm_mem
 
         self.group = group
@@ -36,29 +38,45 @@ class PeerAllReduce:
             raise ValueError(f"peer all-reduce supports up to {_lib.MM_MAX_TP} ranks")
         self.dtype = dtype
         self.device = torch.device(device)
-        self.nblocks = int(nblocks)
         esize = torch.tensor([], dtype=dtype).element_size()
-        gran = 256 // esize  # slots start on 256-byte boundaries
-        self.offsets, self.capacity = [], []
+        gran = 256 // esize  # regions start on 256-byte boundaries
+        self.ll_max_bytes = int(ll_max_bytes)
+        self.offsets, self.capacity, self.strides = [], [], []
         total = 0
         for n in slot_numels:
+            stride = 2 * ((int(n) + gran - 1) // gran * gran)  # room for the low-latency lines
             self.offsets.append(total)
             self.capacity.append(int(n))
-            total += (int(n) + gran - 1) // gran * gran
+            self.strides.append(stride)
+            total += self.world * stride
         self.buf = symm_mem.empty(max(total, gran), dtype=dtype, device=self.device)
         h = symm_mem.rendezvous(self.buf, group)
         self.buf_ptrs = [int(x) for x in h.buffer_ptrs]
-        self.sig = symm_mem.empty(self.nblocks * _lib.MM_MAX_TP, dtype=torch.int32, device=self.device)
+        self.buf.zero_()
+        self.sig = symm_mem.empty(_lib.MM_PEER_MAX_BLOCKS * _lib.MM_MAX_TP, dtype=torch.int32, device=self.device)
         self.sig.zero_()
         hs = symm_mem.rendezvous(self.sig, group)
         self.sig_ptrs = [int(x) for x in hs.buffer_ptrs]
-        self.counters = torch.zeros(self.nblocks + 1, dtype=torch.int32, device=self.device)
+        self.counters = torch.zeros(_lib.MM_PEER_MAX_BLOCKS + 3, dtype=torch.int32, device=self.device)
         self.esize = esize
+        self.vec = 16 // esize
         torch.cuda.synchronize(self.device)
         dist.barrier(group)
 
     def slot(self, site: int) -> torch.Tensor:
-        return self.buf[self.offsets[site]:self.offsets[site] + self.capacity[site]]
+        """This rank's partial of call site `site` (capacity elements)."""
+        off = self.offsets[site] + self.rank * self.strides[site]
+        return self.buf[off:off + self.capacity[site]]
+
+    def protocol(self, n: int) -> int:
+        """Low-latency lines up to ll_max_bytes of partial, the flag protocol above."""
+        return _lib.MM_PEER_LL if n * self.esize <= self.ll_max_bytes else _lib.MM_PEER_FLAGS
+
+    def blocks(self, n: int, protocol: int) -> int:
+        """CTAs for an n-element call: about two 16-byte vectors (flags) or two 8-byte lines (LL) per
+        thread, at most MM_PEER_MAX_BLOCKS."""
+        per_cta = self.THREADS * 2 * (self.vec if protocol == _lib.MM_PEER_FLAGS else 8 // self.esize)
+        return max(1, min(_lib.MM_PEER_MAX_BLOCKS, -(-n // per_cta)))
 
     def reduce(self, site: int, n: int, out: torch.Tensor) -> torch.Tensor:
         if n > self.capacity[site]:
@@ -66,12 +84,14 @@ class PeerAllReduce:
         a = _lib.MMPeerReduceArgs()
         off = self.offsets[site] * self.esize
         for r in range(self.world):
-            a.bufs[r] = self.buf_ptrs[r] + off
+            a.slots[r] = self.buf_ptrs[r] + off
             a.signals[r] = self.sig_ptrs[r]
         a.counters = self.counters.data_ptr()
         a.out = out.data_ptr()
         a.dtype = _lib.DTYPE_CODE[self.dtype]
-        a.n, a.world, a.rank, a.nblocks = n, self.world, self.rank, self.nblocks
+        proto = self.protocol(n)
+        a.n, a.stride, a.world, a.rank = n, self.strides[site], self.world, self.rank
+        a.nblocks, a.protocol = self.blocks(n, proto), proto
         with torch.cuda.device(self.device):
             rc = _lib.lib().mm_peer_allreduce(ctypes.byref(a), _lib.stream_handle(self.device))
         _lib.check(rc, "mm_peer_allreduce")
@@ -79,4 +99,4 @@ class PeerAllReduce:
 
     def timed_out(self) -> bool:
         """True if any wait gave up (a peer never arrived); synchronises the device."""
-        return bool(self.counters[self.nblocks].item())
+        return bool(self.counters[_lib.MM_PEER_MAX_BLOCKS].item())

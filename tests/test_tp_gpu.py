@@ -72,3 +72,62 @@ def test_tp2_matches_single_gpu(peer_rows):
     for p in procs:
         p.join(timeout=60)
     assert all(r[1] and r[2] and r[3] and r[4] for r in res), res
+
+
+def _peer_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from mamba_metal_b200.comm import PeerAllReduce
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        sizes = [1, 7, 100, 12288, 163843]
+        bad = []
+        for dtype, ll_max in ((torch.float32, 1 << 16), (torch.bfloat16, 1 << 16), (torch.bfloat16, 0),
+                              (torch.float16, 1 << 30)):
+            peer = PeerAllReduce(dist.group.WORLD, dev, dtype, sizes, ll_max_bytes=ll_max)
+            for it in range(3):
+                for site, n in enumerate(sizes):
+                    parts = [torch.randn(n, generator=torch.Generator().manual_seed(1000 * it + 10 * site + r))
+                             .to(dtype) for r in range(world)]
+                    peer.slot(site)[:n].copy_(parts[rank])
+                    out = torch.empty(n, dtype=dtype, device=dev)
+                    peer.reduce(site, n, out)
+                    want = parts[0].float()
+                    for r in range(1, world):
+                        want = want + parts[r].float()
+                    if not torch.equal(out.cpu(), want.to(dtype)):
+                        bad.append((str(dtype), ll_max, it, n))
+            if peer.timed_out():
+                bad.append((str(dtype), "timeout"))
+            del peer
+        q.put((rank, bad))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, [repr(e)]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_allreduce_exact():
+    """mm_peer_allreduce on 2 GPUs: ragged and vector sizes, fp32 / bf16 / fp16, both protocols (flags,
+    low-latency lines) and the size-based mix, sites used in rotation; the result equals the rank-ordered
+    fp32 sum rounded to the buffer type, bit for bit."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(not r[1] for r in res), res
