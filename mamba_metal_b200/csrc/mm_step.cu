@@ -1,10 +1,11 @@
 // One-token SSM decode step and the fused residual-add + RMSNorm, for sm_100a.
 //
 // mm_ssm_decode_step restates mamba_metal/mamba_block.py:183-195: dt = softplus(dt_proj(.)),
-// h = exp(dt*A)*h + (dt*x)*B, y = sum_n h*C + D*x, y *= silu(z). One thread owns one (batch, channel)
-// with its dstate states in registers; the fp32 state row (64 bytes for dstate 16) is read and written
-// once with 16-byte vectors, so the step is bound by the state traffic, and A / B / C rows are shared
-// through L1.
+// h = exp(dt*A)*h + (dt*x)*B, y = sum_n h*C + D*x, y *= silu(z). The step is bound by the fp32 state
+// traffic (64 bytes read and written per (batch, channel) at dstate 16). Main kernel (dstate 16, aligned
+// rows): four threads per channel, 16-byte state pieces contiguous across a warp, state and per-row
+// scalars staged by cp.async in two row groups. Other shapes: one thread per (batch, channel) with its
+// dstate states in registers.
 //
 // mm_add_rmsnorm restates the pre-norm residual wrapper of mamba_metal/mamba_model.py:49-58 with
 // nn.RMSNorm (x * rsqrt(mean(x^2) + eps) * weight, eps from :32): residual += delta, then normalise.
@@ -72,6 +73,96 @@ __global__ void __launch_bounds__(128) ssm_step_kernel(const SSMParams p) {
   if (p.D) y = fmaf(p.D[d], xv, y);
   if (p.z) y *= silu(ld_f32(static_cast<const T*>(p.z) + b * p.zsb + d));
   st_f32(static_cast<T*>(p.y) + b * p.ysb + d, y);
+}
+
+// dstate 16, dim a multiple of 8, 16-byte aligned rows: CTA = 32 channels x 16 batch rows in two
+// groups of 8, 128 threads; thread (dl, q) owns states 4q..4q+3 of channel d0 + dl, so a warp's
+// 16-byte state accesses are contiguous. At entry the CTA starts cp.async copies of both groups' state
+// rows and dt / x / z row slices (one commit group each; nothing held in registers), loads B | C with
+// plain loads, then computes group 0 while group 1 is still in flight.
+constexpr int kQdCh = 32, kQdRows = 8, kQdGroups = 2, kQdThreads = 128;
+
+template <typename T>
+struct QuadSmem {
+  float4 h[kQdGroups][kQdRows][kQdThreads];
+  T dxz[kQdGroups][3][kQdRows][kQdCh];  // dt, x, z row slices
+  float bc[kQdGroups][kQdRows][32];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMParams p) {
+  __shared__ __align__(16) QuadSmem<T> sm;
+  constexpr int VE = 16 / sizeof(T);
+  constexpr int kChunks = kQdCh / VE;  // 16-byte chunks per row slice
+  const int tid = threadIdx.x, dl = tid >> 2, q = tid & 3;
+  const int d0 = blockIdx.x * kQdCh, d = d0 + dl;
+  const bool dok = d < p.dim;
+#pragma unroll
+  for (int g = 0; g < kQdGroups; ++g) {
+    const int b0 = (blockIdx.y * kQdGroups + g) * kQdRows;
+    const int nrows = max(0, min(kQdRows, p.batch - b0));
+#pragma unroll
+    for (int r = 0; r < kQdRows; ++r)
+      if (dok && r < nrows)
+        cp_async16(&sm.h[g][r][tid], p.state + ((long long)(b0 + r) * p.dim + d) * 16 + 4 * q);
+    for (int i = tid; i < 3 * kQdRows * kChunks; i += kQdThreads) {
+      const int a = i / (kQdRows * kChunks), rem = i - a * kQdRows * kChunks;
+      const int r = rem / kChunks, c = (rem - r * kChunks) * VE;
+      const T* src = static_cast<const T*>(a == 0 ? p.dt : a == 1 ? p.x : p.z);
+      const long long st = a == 0 ? p.dtsb : a == 1 ? p.xsb : p.zsb;
+      if (r < nrows && d0 + c < p.dim && src) cp_async16(&sm.dxz[g][a][r][c], src + (long long)(b0 + r) * st + d0 + c);
+    }
+    cp_async_commit();
+  }
+  // B | C rows of both groups: row (g, r) by warp (g*8 + r) % 4 ... four warps, sixteen rows
+#pragma unroll
+  for (int j = 0; j < kQdGroups * kQdRows / 4; ++j) {
+    const int gr = j * 4 + (tid >> 5), g = gr / kQdRows, r = gr - g * kQdRows, lane = tid & 31;
+    const int b = (blockIdx.y * kQdGroups + g) * kQdRows + r;
+    float v = 0.f;
+    if (b < p.batch)
+      v = lane < 16 ? ld_f32(static_cast<const T*>(p.B) + (long long)b * p.Bsb + lane)
+                    : ld_f32(static_cast<const T*>(p.C) + (long long)b * p.Csb + (lane - 16));
+    sm.bc[g][r][lane] = v;
+  }
+  const float4 a = dok ? *reinterpret_cast<const float4*>(p.A + (long long)d * 16 + 4 * q) : make_float4(0, 0, 0, 0);
+  const float Dd = (dok && p.D) ? p.D[d] : 0.f;
+#pragma unroll
+  for (int g = 0; g < kQdGroups; ++g) {
+    if (g == 0) cp_async_wait<kQdGroups - 1>();
+    else cp_async_wait<0>();
+    __syncthreads();
+    const int b0 = (blockIdx.y * kQdGroups + g) * kQdRows;
+    const int nrows = max(0, min(kQdRows, p.batch - b0));
+    if (!dok) continue;  // whole warps only (dim % 8 == 0, 8 channels per warp); no barrier follows
+#pragma unroll
+    for (int r = 0; r < kQdRows; ++r) {
+      if (r >= nrows) continue;  // uniform over the CTA
+      const long long b = b0 + r;
+      const float dtv = ElemTraits<T>::to_f32(sm.dxz[g][0][r][dl]);
+      const float xv = ElemTraits<T>::to_f32(sm.dxz[g][1][r][dl]);
+      const float d2 = p.softplus ? softplus_log2(dtv) : dtv * kLog2e;
+      const float du = d2 * kLn2 * xv;
+      const float4 Bv = *reinterpret_cast<const float4*>(&sm.bc[g][r][4 * q]);
+      const float4 Cv = *reinterpret_cast<const float4*>(&sm.bc[g][r][16 + 4 * q]);
+      const float4 h = sm.h[g][r][tid];
+      const f2_t dd = f2_pack(d2, d2), uu = f2_pack(du, du);
+      const float2 e01 = f2_unpack(f2_mul(dd, f2_pack(a.x, a.y))), e23 = f2_unpack(f2_mul(dd, f2_pack(a.z, a.w)));
+      const f2_t h01 = f2_fma(f2_pack(ex2(e01.x), ex2(e01.y)), f2_pack(h.x, h.y), f2_mul(uu, f2_pack(Bv.x, Bv.y)));
+      const f2_t h23 = f2_fma(f2_pack(ex2(e23.x), ex2(e23.y)), f2_pack(h.z, h.w), f2_mul(uu, f2_pack(Bv.z, Bv.w)));
+      const float2 n01 = f2_unpack(h01), n23 = f2_unpack(h23);
+      *reinterpret_cast<float4*>(p.state + (b * p.dim + d) * 16 + 4 * q) = make_float4(n01.x, n01.y, n23.x, n23.y);
+      const float2 yy = f2_unpack(f2_fma(h23, f2_pack(Cv.z, Cv.w), f2_mul(h01, f2_pack(Cv.x, Cv.y))));
+      float y = yy.x + yy.y;
+      y += __shfl_xor_sync(0xffffffffu, y, 1);
+      y += __shfl_xor_sync(0xffffffffu, y, 2);
+      if (q == 0) {
+        y = fmaf(Dd, xv, y);
+        if (p.z) y *= silu(ElemTraits<T>::to_f32(sm.dxz[g][2][r][dl]));
+        st_f32(static_cast<T*>(p.y) + b * p.ysb + d, y);
+      }
+    }
+  }
 }
 
 struct NormParams {
@@ -183,6 +274,7 @@ static cudaError_t launch_norm(const NormParams& p, bool vec, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+
 }  // namespace step
 }  // namespace mm
 
@@ -203,6 +295,18 @@ extern "C" int mm_ssm_decode_step(const MMSSMStepArgs* a, mm_stream_t stream) {
   p.batch = (int)a->batch; p.dim = (int)a->dim; p.nstate = (int)a->dstate; p.softplus = a->dt_softplus != 0;
   p.vec = aligned16(a->ssm_state) && aligned16(a->A) && a->dstate == 16;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t es = dtype_size(a->dtype);
+  const bool rows16 = aligned16(a->x) && aligned16(a->dt) && (!a->z || aligned16(a->z)) &&
+                      (a->x_stride_b * (int64_t)es) % 16 == 0 && (a->dt_stride_b * (int64_t)es) % 16 == 0 &&
+                      (!a->z || (a->z_stride_b * (int64_t)es) % 16 == 0);
+  if (p.vec && p.dim % 8 == 0 && rows16) {
+    const int rows_per_cta = step::kQdRows * step::kQdGroups;
+    const dim3 qgrid((p.dim + step::kQdCh - 1) / step::kQdCh, (p.batch + rows_per_cta - 1) / rows_per_cta);
+    if (a->dtype == MM_F32) step::ssm_step_quad_kernel<float><<<qgrid, step::kQdThreads, 0, s>>>(p);
+    else if (a->dtype == MM_F16) step::ssm_step_quad_kernel<__half><<<qgrid, step::kQdThreads, 0, s>>>(p);
+    else step::ssm_step_quad_kernel<__nv_bfloat16><<<qgrid, step::kQdThreads, 0, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? MM_OK : MM_ERR_LAUNCH;
+  }
   const dim3 grid((p.dim + 127) / 128, p.batch);
   // the NM = 16 instantiation handles any dstate through its scalar branch when not vectorisable
   if (a->dtype == MM_F32) step::ssm_step_kernel<float, 16><<<grid, 128, 0, s>>>(p);

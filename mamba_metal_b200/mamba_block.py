@@ -112,8 +112,8 @@ class MambaBlock(nn.Module):
         xz = F.linear(x_token[:, 0].to(dt_), self.in_proj.weight)       # (B, 2E)
         xc = ops.causal_conv1d_step(xz[:, :E], conv_state, self.conv1d.weight, self.conv1d.bias, silu=True)
         x_dbl = self._project(xc, self.x_proj.weight, 0)                    # (B, R + 2N)
-        dt = F.linear(x_dbl[:, :R], self.dt_proj.weight, self.dt_proj.bias)
         Df = self.D if self.D.dtype == torch.float32 else self.D.float()
-        y = ops.ssm_decode_step(xc, dt, xz[:, E:], x_dbl[:, R:R + N], x_dbl[:, R + N:], self._A(), Df, ssm_state,
-                                dt_softplus=True)
+        dt = F.linear(x_dbl[:, :R], self.dt_proj.weight, self.dt_proj.bias)
+        y = ops.ssm_decode_step(xc, dt, xz[:, E:], x_dbl[:, R:R + N], x_dbl[:, R + N:], self._A(), Df,
+                                ssm_state, dt_softplus=True)
         return self._project(y, self.out_proj.weight, 1)[:, None, :], conv_state, ssm_state

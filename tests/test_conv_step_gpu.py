@@ -75,8 +75,11 @@ def test_conv_step_matches_prefill(dtype):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("n", [16, 8, 5])
-def test_ssm_step_chain_matches_scan(dtype, n):
-    b, d, L = 3, 50, 20
+@pytest.mark.parametrize("b,d", [(3, 50), (9, 136)])
+def test_ssm_step_chain_matches_scan(dtype, n, b, d):
+    """A chain of decode steps equals the scan (dstate 16 with dim % 8 == 0 takes the coalesced
+    4-threads-per-channel kernel; the other shapes the one-thread-per-channel kernel)."""
+    L = 20
     inp = R.make_features_inputs(b, d, n, L, seed=n)
     qq = {k: (q(v, dtype) if k in ("u", "delta", "B", "C", "z") else v) for k, v in inp.items()}
     yr, hr = R.selective_scan_vec(**qq, delta_softplus=True, return_state=True, dtype=np.float64)
