@@ -320,6 +320,125 @@ def _dist_tools(dev, world):
     return sync_all, max_over_ranks
 
 
+LONG = dict(batch=4, dim=5120, dstate=16, seqlen=131072)
+LONG_BLOCK = 640  # channels per generator seed: the global inputs are the same for every rank count
+
+
+def make_long_inputs(dev, c0, c1, seed=0):
+    """BASELINE configs[4] inputs for channels [c0, c1) (multiples of LONG_BLOCK), generated on the device
+    (2.7 G elements: host generation would take minutes): u ~ N(0,1), delta ~ N(0,1)*0.5 (raw, softplus),
+    z ~ N(0,1), D ~ N(0,1) per channel block from torch.Generator(seed * 100003 + block); B, C ~ N(0,1)
+    (batch, 16, seqlen) from seed * 100003 + 99999; A[d,n] = -(n+1). u/delta/z/B/C fp16, A/D fp32."""
+    import torch
+
+    b, n, L = LONG["batch"], LONG["dstate"], LONG["seqlen"]
+    assert c0 % LONG_BLOCK == 0 and c1 % LONG_BLOCK == 0
+    out = {k: torch.empty((b, c1 - c0, L), dtype=torch.float16, device=dev) for k in ("u", "delta", "z")}
+    D = torch.empty(c1 - c0, dtype=torch.float32, device=dev)
+    for blk in range(c0 // LONG_BLOCK, c1 // LONG_BLOCK):
+        g = torch.Generator(device=dev).manual_seed(seed * 100003 + blk)
+        sl = slice(blk * LONG_BLOCK - c0, (blk + 1) * LONG_BLOCK - c0)
+        for k, scale in (("u", 1.0), ("delta", 0.5), ("z", 1.0)):
+            out[k][:, sl] = (torch.randn((b, LONG_BLOCK, L), generator=g, device=dev) * scale).half()
+        D[sl] = torch.randn(LONG_BLOCK, generator=g, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed * 100003 + 99999)
+    out["B"] = torch.randn((b, n, L), generator=g, device=dev).half()
+    out["C"] = torch.randn((b, n, L), generator=g, device=dev).half()
+    out["D"] = D
+    out["A"] = -torch.arange(1, n + 1, dtype=torch.float32, device=dev).repeat(c1 - c0, 1)
+    return out
+
+
+def cpu_long_rate(budget_s=10.0, seed=0):
+    """The C oracle (all host threads) on whole configs[4]-length rows: as many (batch, channel) rows of
+    131,072 steps as fit the time budget; returns (Gelem/s, threads, sample description)."""
+    from oracle.scan_c import max_threads, selective_scan_c
+
+    threads = max_threads()
+    L = LONG["seqlen"]
+    rng = np.random.default_rng(seed)
+
+    def run(rows):
+        u = rng.standard_normal((1, rows, L), dtype=np.float32)
+        dl = rng.standard_normal((1, rows, L), dtype=np.float32) * np.float32(0.5)
+        z = rng.standard_normal((1, rows, L), dtype=np.float32)
+        Bm = rng.standard_normal((1, 16, L), dtype=np.float32)
+        Cm = rng.standard_normal((1, 16, L), dtype=np.float32)
+        A = -np.broadcast_to(np.arange(1, 17, dtype=np.float32), (rows, 16)).copy()
+        D = rng.standard_normal(rows, dtype=np.float32)
+        t0 = time.perf_counter()
+        selective_scan_c(u, dl, A, Bm, Cm, D, z, delta_softplus=True, threads=threads)
+        return time.perf_counter() - t0
+
+    dt = run(threads)
+    rows = int(max(threads, min(1024, threads * budget_s / max(dt, 1e-3))))
+    dt = run(rows)
+    return rows * L / dt / 1e9, threads, (f"configs[4]-length rows: {rows} (batch, channel) rows x {L} steps "
+                                          f"({rows * L} elements, {dt:.1f} s), BASELINE distributions, fp32")
+
+
+def run_long(args, rank, world, local_rank):
+    """configs[4]: long-context selective scan, fp16 (4, 5120, 131072), N 16, D / z / softplus, final state;
+    channel-sharded: rank r scans channels [r*5120/N, (r+1)*5120/N) with no communication (B and C are
+    replicated). Strong scaling: the value is the whole problem's element rate."""
+    import torch
+
+    from mamba_metal_b200.selective_scan import selective_scan_into
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    sync_all, max_over_ranks = _dist_tools(dev, world)
+    b, dm, n, L = LONG["batch"], LONG["dim"], LONG["dstate"], LONG["seqlen"]
+    if dm % (world * LONG_BLOCK) != 0:
+        raise SystemExit(f"configs[4] shards {dm} channels in blocks of {LONG_BLOCK}: world {world} unsupported")
+    shard = dm // world
+    c0 = rank * shard
+    d = make_long_inputs(dev, c0, c0 + shard)
+    y = torch.empty((b, shard, L), dtype=torch.float16, device=dev)
+    state = torch.empty((b, shard, n), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        selective_scan_into(d["u"], d["delta"], d["A"], d["B"], d["C"], d["D"], d["z"], y, state, True)
+
+    for _ in range(args.warmup):
+        step()
+    sync_all()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    with ClockSampler(_nvml_index(local_rank)) as clk:
+        sync_all()
+        for k in range(args.steps):
+            ev[2 * k].record(stream)
+            step()
+            ev[2 * k + 1].record(stream)
+        sync_all()
+    total_ms = max_over_ranks(ev[0].elapsed_time(ev[-1]))
+    launch_ms = max_over_ranks(statistics.mean(ev[2 * k].elapsed_time(ev[2 * k + 1]) for k in range(args.steps)))
+    if rank != 0:
+        return
+    ms = total_ms / args.steps
+    peak, kind = load_peaks()
+    per_rank_bytes = scan_bytes(b, shard, n, L)
+    achieved = per_rank_bytes / (launch_ms * 1e-3) / 1e9
+    cpu = None
+    if world == 1 and not args.no_extras:
+        rate, threads, sample = cpu_long_rate()
+        cpu = {"value": rate, "unit": "Gelem/s", "cores": threads, "kind": "port", "sample": sample}
+    print(json.dumps({
+        "metric": METRIC, "value": b * dm * L / (ms * 1e-3) / 1e9, "unit": "Gelem/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 in / f32 math",
+        "data": "synthetic (BASELINE configs[4] distributions, on-device seeded generators)",
+        "config": {"workload": "selective_scan configs[4]: long context, channel-sharded, no communication",
+                   **LONG, "channels_per_gpu": shard, "l2": "inputs larger than L2 (21.5 GB per step at N=1)"},
+        "aggregate_hbm_gbs": world * per_rank_bytes / (ms * 1e-3) / 1e9,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_kind": kind, "algorithmic_bytes": per_rank_bytes, "launch_ms": launch_ms},
+        "cpu_baseline": cpu,
+        "e2e": None, "e2e_note": "not measured for configs[4]: 16 GB of pinned host inputs per step",
+        "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
+
+
 def run_conv(args, rank, world, local_rank):
     """configs[1] causal conv1d: fp16 x (8, 1536, 4096) channel-first, w (1536, 4) ~ U(-.5,.5),
     bias ~ U(-.1,.1), no activation (BASELINE states none); every rank runs the same batch (weak)."""
@@ -462,9 +581,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="device loop only: no e2e arm, no CPU baseline")
-    ap.add_argument("--workload", choices=["scan", "conv", "decode"], default="scan",
+    ap.add_argument("--workload", choices=["scan", "conv", "decode", "long"], default="scan",
                     help="scan: configs[1] selective scan (default, the headline); conv: configs[1] causal conv1d; "
-                         "decode: configs[3] Mamba-2.8b-architecture batch-64 decode, tensor-parallel at N > 1")
+                         "decode: configs[3] Mamba-2.8b-architecture batch-64 decode, tensor-parallel at N > 1; "
+                         "long: configs[4] long-context scan, channel-sharded at N > 1")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -482,7 +602,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        {"scan": run_ours, "conv": run_conv, "decode": run_decode}[args.workload](args, rank, world, local_rank)
+        {"scan": run_ours, "conv": run_conv, "decode": run_decode, "long": run_long}[args.workload](
+            args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

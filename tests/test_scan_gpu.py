@@ -224,3 +224,25 @@ def test_deterministic_and_l2_independent():
     y1, h1 = run(inp, torch.float16)
     y2, h2 = run(inp, torch.float16)
     assert torch.equal(y1, y2) and torch.equal(h1, h2)
+
+
+def test_config4_long_context_final_state():
+    """fp16 (4, 5120, 131072), N 16, D / z / softplus, the inputs bench.py's `long`
+    workload times (on-device seeded generators). Six sampled (batch, channel) rows -- all 131,072 outputs
+    and the final state -- against the C oracle on the same fp16-rounded inputs, in fp32."""
+    import bench
+    from oracle.scan_c import selective_scan_c
+
+    dev = torch.device(DEV)
+    d = bench.make_long_inputs(dev, 0, bench.LONG["dim"])
+    y, h = selective_scan(d["u"], d["delta"], d["A"], d["B"], d["C"], D=d["D"], z=d["z"], delta_softplus=True,
+                          return_state=True)
+    for b, c in [(0, 0), (1, 777), (2, 2560), (3, 5119), (0, 4001), (3, 1234)]:
+        row = lambda t: np.ascontiguousarray(t[b:b + 1, c:c + 1].float().cpu().numpy())
+        yr, hr = selective_scan_c(row(d["u"]), row(d["delta"]), d["A"][c:c + 1].cpu().numpy(),
+                                  d["B"][b:b + 1].float().cpu().numpy(), d["C"][b:b + 1].float().cpu().numpy(),
+                                  d["D"][c:c + 1].cpu().numpy(), row(d["z"]), delta_softplus=True)
+        assert_close(h[b, c], hr[0, 0], 2e-3, f"final state ({b},{c})")
+        assert_close(y[b, c].float(), yr[0, 0], 2e-3, f"y ({b},{c})")
+    del d, y, h
+    torch.cuda.empty_cache()
