@@ -7,6 +7,7 @@ checkpoints offline) and ``load_kernel`` (the MLX Metal loader) has no counterpa
 """
 
 from mamba_metal_b200.generate import GraphDecoder, generate, generate_fast, generate_ids
+from mamba_metal_b200.load_hf import load_mamba_hf
 from mamba_metal_b200.mamba_block import MambaBlock
 from mamba_metal_b200.mamba_model import MambaConfig, MambaModel, MambaResidualBlock, RMSNorm, init_weights_
 from mamba_metal_b200.ops import add_rmsnorm, causal_conv1d, causal_conv1d_step, ssm_decode_step
@@ -25,6 +26,7 @@ __all__ = [
     "generate",
     "generate_fast",
     "generate_ids",
+    "load_mamba_hf",
     "init_weights_",
     "selective_scan",
     "ssm_decode_step",
