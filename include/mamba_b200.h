@@ -3,9 +3,10 @@
  *
  * The library is libmamba_b200.so (built from mamba_metal_b200/csrc/). Every entry point takes a
  * plain argument struct of device pointers, element strides and sizes, plus a CUDA stream handle,
- * and returns MM_OK (0) or a negative MM_ERR_* code. No entry point aborts, allocates device memory
- * or keeps hidden mutable state: the caller owns every buffer (outputs and workspace), and all work
- * is ordered on the given stream. Integer fields are int64_t so the struct layout is the same for
+ * and returns MM_OK (0) or a negative MM_ERR_* code. No entry point aborts or allocates device memory,
+ * and none keeps hidden mutable state except the fixed scratch buffer of mm_selective_scan_fwd_noalloc:
+ * the caller owns every other buffer (outputs and workspace), and all work is ordered on the given
+ * stream. Integer fields are int64_t so the struct layout is the same for
  * every FFI (ctypes, cgo, JNI) without padding surprises.
  *
  * Reference interface being replaced (createcentury/mamba-metal):
@@ -254,6 +255,26 @@ typedef struct MMPeerReduceArgs {
 } MMPeerReduceArgs;
 
 int mm_peer_allreduce(const MMPeerReduceArgs* args, mm_stream_t stream);
+
+/* The low-latency all-reduce of a (rows, dim) partial fused with the residual add + RMSNorm that
+ * follows the out_proj reduction in a tensor-parallel decode step (mamba_model.py:49-58 with
+ * nn.RMSNorm): per row, s = sum over ranks (fp32, rank order) rounded to `dtype`;
+ * residual += s (fp32, in place); out = residual * rsqrt(mean(residual^2) + eps) * weight.
+ * reduce.protocol must be MM_PEER_LL, reduce.n = rows * dim, reduce.out is unused; dim * element size
+ * a multiple of 8 bytes and at most 16 KiB; residual (rows, dim) fp32 contiguous, 16-byte aligned;
+ * weight (dim,) fp32; out (rows, dim) of `dtype` with row stride out_stride_r. One CTA per row
+ * (reduce.nblocks only has to be in range); it shares the LL epoch counter with mm_peer_allreduce (one
+ * sequence of calls). */
+typedef struct MMPeerAddNormArgs {
+  MMPeerReduceArgs reduce;
+  float* residual;
+  const float* weight;
+  void* out;
+  int64_t rows, dim, out_stride_r;
+  double eps;
+} MMPeerAddNormArgs;
+
+int mm_peer_allreduce_add_rmsnorm(const MMPeerAddNormArgs* args, mm_stream_t stream);
 
 /* Library version string (static storage). */
 const char* mm_version(void);

@@ -85,6 +85,13 @@ class MMPeerReduceArgs(ctypes.Structure):
     ]
 
 
+class MMPeerAddNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("reduce", MMPeerReduceArgs), ("residual", _p), ("weight", _p), ("out", _p), ("rows", _i64),
+        ("dim", _i64), ("out_stride_r", _i64), ("eps", ctypes.c_double),
+    ]
+
+
 _SIGNATURES = {
     "mm_selective_scan_workspace_size": ([ctypes.POINTER(MMScanArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "mm_selective_scan_fwd": ([ctypes.POINTER(MMScanArgs), _p, ctypes.c_size_t, _p], ctypes.c_int),
@@ -96,6 +103,7 @@ _SIGNATURES = {
     "mm_ssm_decode_step": ([ctypes.POINTER(MMSSMStepArgs), _p], ctypes.c_int),
     "mm_add_rmsnorm": ([ctypes.POINTER(MMAddNormArgs), _p], ctypes.c_int),
     "mm_peer_allreduce": ([ctypes.POINTER(MMPeerReduceArgs), _p], ctypes.c_int),
+    "mm_peer_allreduce_add_rmsnorm": ([ctypes.POINTER(MMPeerAddNormArgs), _p], ctypes.c_int),
     "mm_version": ([], ctypes.c_char_p),
 }
 

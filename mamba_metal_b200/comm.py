@@ -78,7 +78,7 @@ class PeerAllReduce:
         per_cta = self.THREADS * 2 * (self.vec if protocol == _lib.MM_PEER_FLAGS else 8 // self.esize)
         return max(1, min(_lib.MM_PEER_MAX_BLOCKS, -(-n // per_cta)))
 
-    def reduce(self, site: int, n: int, out: torch.Tensor) -> torch.Tensor:
+    def _args(self, site: int, n: int, proto: int) -> "_lib.MMPeerReduceArgs":
         if n > self.capacity[site]:
             raise ValueError("partial larger than its slot")
         a = _lib.MMPeerReduceArgs()
@@ -87,14 +87,32 @@ class PeerAllReduce:
             a.slots[r] = self.buf_ptrs[r] + off
             a.signals[r] = self.sig_ptrs[r]
         a.counters = self.counters.data_ptr()
-        a.out = out.data_ptr()
         a.dtype = _lib.DTYPE_CODE[self.dtype]
-        proto = self.protocol(n)
         a.n, a.stride, a.world, a.rank = n, self.strides[site], self.world, self.rank
         a.nblocks, a.protocol = self.blocks(n, proto), proto
+        return a
+
+    def reduce(self, site: int, n: int, out: torch.Tensor) -> torch.Tensor:
+        a = self._args(site, n, self.protocol(n))
+        a.out = out.data_ptr()
         with torch.cuda.device(self.device):
             rc = _lib.lib().mm_peer_allreduce(ctypes.byref(a), _lib.stream_handle(self.device))
         _lib.check(rc, "mm_peer_allreduce")
+        return out
+
+    def reduce_add_rmsnorm(self, site: int, rows: int, dim: int, residual: torch.Tensor, weight: torch.Tensor,
+                           eps: float, out: torch.Tensor) -> torch.Tensor:
+        """Sums the (rows, dim) partials of site `site` (low-latency protocol), adds the sum (rounded to the
+        buffer dtype) into the fp32 `residual` in place and writes RMSNorm(residual) * weight to `out`."""
+        assert residual.is_contiguous() and residual.dtype == torch.float32 and residual.numel() == rows * dim
+        assert weight.dtype == torch.float32 and out.dtype == self.dtype and out.is_contiguous()
+        a = _lib.MMPeerAddNormArgs()
+        a.reduce = self._args(site, rows * dim, _lib.MM_PEER_LL)
+        a.residual, a.weight, a.out = residual.data_ptr(), weight.data_ptr(), out.data_ptr()
+        a.rows, a.dim, a.out_stride_r, a.eps = rows, dim, dim, float(eps)
+        with torch.cuda.device(self.device):
+            rc = _lib.lib().mm_peer_allreduce_add_rmsnorm(ctypes.byref(a), _lib.stream_handle(self.device))
+        _lib.check(rc, "mm_peer_allreduce_add_rmsnorm")
         return out
 
     def timed_out(self) -> bool:

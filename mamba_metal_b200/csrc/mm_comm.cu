@@ -218,12 +218,134 @@ __global__ void __launch_bounds__(kThreads) peer_allreduce_kernel(const Params p
   if (tid == 0) p.counters[c] = e;
 }
 
+
+// Low-latency all-reduce fused with the residual add + RMSNorm that follows it (the out_proj reduction
+// of a tensor-parallel decode step feeding the next pre-norm, mamba_model.py:49-58). CTA r owns row r:
+// it pushes the row's lines, sums every rank's lines in rank order, rounds the sum to T (as the unfused
+// all-reduce output would be), adds it into the fp32 residual, and writes the normalised row. Epochs as
+// in peer_allreduce_ll_kernel (the two kernels share the counter: one sequence of LL calls).
+constexpr int kNormMaxLines = 8;  // per thread: rows up to 8 x 256 lines
+
+struct NormArgs {
+  float* res;
+  const float* w;
+  void* out;
+  long long osr;
+  int dim;
+  float eps;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) peer_ll_addnorm_kernel(const Params p, const NormArgs q) {
+  constexpr int E = 4 / sizeof(T);  // elements per word
+  constexpr int LE = 2 * E;         // elements per line
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int lines = q.dim / LE;
+  const long long l0 = (long long)row * lines;
+  const long long own = (long long)p.rank * p.stride;
+  const uint2* mine = reinterpret_cast<const uint2*>(static_cast<const T*>(p.slots[p.rank]) + own);
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(p.counters + kLLEpoch) + 1u;
+  for (int j = tid; j < lines; j += kThreads) {
+    const uint2 w = mine[l0 + j];
+    const uint4 line = make_uint4(w.x, e, w.y, e);
+    for (int r = 0; r < p.world; ++r)
+      if (r != p.rank) st_volatile_v4(reinterpret_cast<uint4*>(static_cast<T*>(p.slots[r]) + own) + l0 + j, line);
+  }
+  const T* area = static_cast<const T*>(p.slots[p.rank]);
+  float* res = q.res + (long long)row * q.dim;
+  float v[kNormMaxLines][LE];
+  float ss = 0.f;
+  bool gave_up = false;
+#pragma unroll
+  for (int i = 0; i < kNormMaxLines; ++i) {
+    const int j = tid + i * kThreads;
+    if (j >= lines) break;
+    float acc[LE];
+#pragma unroll
+    for (int k = 0; k < LE; ++k) acc[k] = 0.f;
+    for (int r = 0; r < p.world; ++r) {
+      uint2 w;
+      if (r == p.rank) {
+        w = mine[l0 + j];
+      } else {
+        const uint4* src = reinterpret_cast<const uint4*>(area + (long long)r * p.stride) + l0 + j;
+        uint4 x = ld_volatile_v4(src);
+        if ((x.y != e || x.w != e) && !gave_up) {
+          const unsigned long long t0 = globaltimer_ns();
+          do {
+            __nanosleep(20);
+            x = ld_volatile_v4(src);
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              atomicOr(p.counters + kErrWord, 1u);  // a peer never arrived: report, do not hang
+              gave_up = true;
+              break;
+            }
+          } while (x.y != e || x.w != e);
+        }
+        w = make_uint2(x.x, x.z);
+      }
+      const float2 a = word_f2<T>(w.x), b = word_f2<T>(w.y);
+      acc[0] += a.x;
+      acc[E] += b.x;
+      if (E == 2) {
+        acc[1] += a.y;
+        acc[E + 1] += b.y;
+      }
+    }
+    float* rp = res + j * LE;
+    float rv[LE];
+    if (LE == 4) {
+      const float4 r4 = *reinterpret_cast<const float4*>(rp);
+      rv[0] = r4.x; rv[1] = r4.y; rv[LE > 2 ? 2 : 0] = r4.z; rv[LE > 3 ? 3 : 0] = r4.w;
+    } else {
+      const float2 r2 = *reinterpret_cast<const float2*>(rp);
+      rv[0] = r2.x; rv[1] = r2.y;
+    }
+#pragma unroll
+    for (int k = 0; k < LE; ++k) {
+      v[i][k] = rv[k] + ElemTraits<T>::to_f32(ElemTraits<T>::from_f32(acc[k]));
+      ss = fmaf(v[i][k], v[i][k], ss);
+    }
+    if (LE == 4) *reinterpret_cast<float4*>(rp) = make_float4(v[i][0], v[i][1], v[i][LE > 2 ? 2 : 0], v[i][LE > 3 ? 3 : 0]);
+    else *reinterpret_cast<float2*>(rp) = make_float2(v[i][0], v[i][1]);
+  }
+  // block sum of squares
+  __shared__ float red[kThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  if (tid < 32) {
+    float t = tid < kThreads / 32 ? red[tid] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (tid == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)q.dim + q.eps);
+  T* out = static_cast<T*>(q.out) + (long long)row * q.osr;
+#pragma unroll
+  for (int i = 0; i < kNormMaxLines; ++i) {
+    const int j = tid + i * kThreads;
+    if (j >= lines) break;
+#pragma unroll
+    for (int k = 0; k < LE; ++k) st_f32(out + j * LE + k, v[i][k] * inv * q.w[j * LE + k]);
+  }
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(p.counters + kLLTicket, 1u) == gridDim.x - 1u) {
+      p.counters[kLLTicket] = 0u;
+      p.counters[kLLEpoch] = e;
+    }
+  }
+}
+
 }  // namespace comm
 }  // namespace mm
 
 using namespace mm;
 
-extern "C" int mm_peer_allreduce(const MMPeerReduceArgs* a, mm_stream_t stream) {
+static int fill_params(const MMPeerReduceArgs* a, comm::Params& p) {
   if (!a) return MM_ERR_ARG;
   const size_t es = dtype_size(a->dtype);
   if (es == 0) return MM_ERR_DTYPE;
@@ -233,15 +355,12 @@ extern "C" int mm_peer_allreduce(const MMPeerReduceArgs* a, mm_stream_t stream) 
   if (a->protocol != MM_PEER_FLAGS && a->protocol != MM_PEER_LL) return MM_ERR_ARG;
   // an LL area holds 16 bytes per 8 data bytes
   if (a->protocol == MM_PEER_LL && (a->n * (int64_t)es + 7) / 8 * 16 > a->stride * (int64_t)es) return MM_ERR_SHAPE;
-  if (!a->counters || !a->out) return MM_ERR_ARG;
-  comm::Params p;
+  if (!a->counters) return MM_ERR_ARG;
   for (int r = 0; r < MM_MAX_TP; ++r) {
     p.slots[r] = r < a->world ? a->slots[r] : nullptr;
     p.signals[r] = r < a->world ? a->signals[r] : nullptr;
     if (r < a->world && (!a->slots[r] || !a->signals[r] || !aligned16(a->slots[r]))) return MM_ERR_ARG;
   }
-  if (!aligned16(a->out)) return MM_ERR_ARG;
-  if (a->n == 0) return MM_OK;
   p.counters = a->counters;
   p.out = a->out;
   p.n = a->n;
@@ -249,6 +368,15 @@ extern "C" int mm_peer_allreduce(const MMPeerReduceArgs* a, mm_stream_t stream) 
   p.world = (int)a->world;
   p.rank = (int)a->rank;
   p.nblocks = (int)a->nblocks;
+  return MM_OK;
+}
+
+extern "C" int mm_peer_allreduce(const MMPeerReduceArgs* a, mm_stream_t stream) {
+  comm::Params p;
+  const int rc = fill_params(a, p);
+  if (rc != MM_OK) return rc;
+  if (!a->out || !aligned16(a->out)) return MM_ERR_ARG;
+  if (a->n == 0) return MM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a->protocol == MM_PEER_LL) {
     if (a->dtype == MM_F32) comm::peer_allreduce_ll_kernel<float><<<p.nblocks, comm::kThreads, 0, s>>>(p);
@@ -261,5 +389,35 @@ extern "C" int mm_peer_allreduce(const MMPeerReduceArgs* a, mm_stream_t stream) 
   } else {
     comm::peer_allreduce_kernel<__nv_bfloat16><<<p.nblocks, comm::kThreads, 0, s>>>(p);
   }
+  return cudaGetLastError() == cudaSuccess ? MM_OK : MM_ERR_LAUNCH;
+}
+
+extern "C" int mm_peer_allreduce_add_rmsnorm(const MMPeerAddNormArgs* a, mm_stream_t stream) {
+  if (!a) return MM_ERR_ARG;
+  comm::Params p;
+  const int rc = fill_params(&a->reduce, p);
+  if (rc != MM_OK) return rc;
+  const int64_t es = (int64_t)dtype_size(a->reduce.dtype);
+  const int64_t le = 8 / es;  // elements per low-latency line
+  if (a->reduce.protocol != MM_PEER_LL) return MM_ERR_ARG;
+  if (a->rows < 0 || a->dim < 1 || a->dim % le != 0 || a->dim / le > comm::kNormMaxLines * comm::kThreads)
+    return MM_ERR_SHAPE;
+  if (a->reduce.n != a->rows * a->dim || a->rows > (1LL << 31) - 1) return MM_ERR_SHAPE;
+  if (!a->residual || !a->weight || !a->out) return MM_ERR_ARG;
+  if (!aligned16(a->residual)) return MM_ERR_ARG;
+  if (a->rows == 0) return MM_OK;
+  p.nblocks = (int)a->rows;
+  comm::NormArgs q;
+  q.res = a->residual;
+  q.w = a->weight;
+  q.out = a->out;
+  q.osr = a->out_stride_r;
+  q.dim = (int)a->dim;
+  q.eps = (float)a->eps;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)a->rows;
+  if (a->reduce.dtype == MM_F32) comm::peer_ll_addnorm_kernel<float><<<grid, comm::kThreads, 0, s>>>(p, q);
+  else if (a->reduce.dtype == MM_F16) comm::peer_ll_addnorm_kernel<__half><<<grid, comm::kThreads, 0, s>>>(p, q);
+  else comm::peer_ll_addnorm_kernel<__nv_bfloat16><<<grid, comm::kThreads, 0, s>>>(p, q);
   return cudaGetLastError() == cudaSuccess ? MM_OK : MM_ERR_LAUNCH;
 }

@@ -100,7 +100,8 @@ class MambaBlock(nn.Module):
         d_state) fp32) -- mamba_block.py:104-153."""
         return self._run(x, want_state=True)
 
-    def step(self, x_token: torch.Tensor, conv_state: torch.Tensor, ssm_state: torch.Tensor, inplace: bool = False):
+    def step(self, x_token: torch.Tensor, conv_state: torch.Tensor, ssm_state: torch.Tensor, inplace: bool = False,
+             defer_out: bool = False):
         """O(1) per-token forward (mamba_block.py:155-198). x_token: (B, 1, d_model).
         Returns (y (B, 1, d_model), new_conv_state, new_ssm_state)."""
         E, N, R = self.d_inner, self.d_state, self.dt_rank
@@ -116,4 +117,9 @@ class MambaBlock(nn.Module):
         dt = F.linear(x_dbl[:, :R], self.dt_proj.weight, self.dt_proj.bias)
         y = ops.ssm_decode_step(xc, dt, xz[:, E:], x_dbl[:, R:R + N], x_dbl[:, R + N:], self._A(), Df,
                                 ssm_state, dt_softplus=True)
+        if defer_out and self.tp_reduce is not None and hasattr(self.tp_reduce, "partial"):
+            # tensor parallel: leave out_proj's all-reduce to the caller's fused residual add + RMSNorm
+            pending = self.tp_reduce.partial(y, self.out_proj.weight, self.tp_sites[1])
+            if pending is not None:
+                return pending, conv_state, ssm_state
         return self._project(y, self.out_proj.weight, 1)[:, None, :], conv_state, ssm_state

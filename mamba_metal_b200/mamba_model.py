@@ -103,10 +103,13 @@ class MambaModel(nn.Module):
                 new_conv.append(cs)
                 new_ssm.append(ss)
             else:
-                y, cs, ss = layer.mixer.step(h, conv_states[i], ssm_states[i], inplace=inplace)
+                y, cs, ss = layer.mixer.step(h, conv_states[i], ssm_states[i], inplace=inplace, defer_out=True)
                 new_conv.append(cs)
                 new_ssm.append(ss)
-            h = ops.add_rmsnorm(residual, y, self._norm_weight(i + 1), eps, self.dtype)
+            if hasattr(y, "add_rmsnorm"):  # tensor-parallel out_proj partial: all-reduce + add + norm fused
+                h = y.add_rmsnorm(residual, self._norm_weight(i + 1), eps, self.dtype)
+            else:
+                h = ops.add_rmsnorm(residual, y, self._norm_weight(i + 1), eps, self.dtype)
         if last_only:
             h = h[:, -1:, :]
         logits = F.linear(h, self.embeddings.weight)            # tied head (mamba_model.py:76-78)

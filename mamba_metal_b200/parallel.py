@@ -76,6 +76,31 @@ class _TPProject:
         dist.all_reduce(t32, group=self.group)
         return t32.to(x.dtype)
 
+    def partial(self, x: torch.Tensor, w: torch.Tensor, site: int):
+        """Writes this rank's x @ w.T into the site's peer slot and returns a _PendingReduce whose
+        add_rmsnorm finishes the all-reduce fused with the next residual add + RMSNorm; None when the
+        call does not take the peer path (then the caller reduces as usual)."""
+        rows = x.numel() // x.shape[-1]
+        n = rows * w.shape[0]
+        peer = self.peer
+        if peer is None or rows > self.max_rows or x.dtype != peer.dtype or n > peer.capacity[site] \
+                or n * peer.esize > peer.ll_max_bytes:
+            return None
+        part = peer.slot(site)[:n].view(rows, w.shape[0])
+        torch.matmul(x.reshape(rows, x.shape[-1]), w.t(), out=part)
+        return _PendingReduce(peer, site, rows, w.shape[0])
+
+
+class _PendingReduce:
+    """An out_proj partial already in its peer slot, reduced by the next pre-norm (mamba_model.py:49-58)."""
+
+    def __init__(self, peer, site: int, rows: int, dim: int):
+        self.peer, self.site, self.rows, self.dim = peer, site, rows, dim
+
+    def add_rmsnorm(self, residual: torch.Tensor, weight: torch.Tensor, eps: float, out_dtype: torch.dtype):
+        out = torch.empty(residual.shape, dtype=out_dtype, device=residual.device)
+        return self.peer.reduce_add_rmsnorm(self.site, self.rows, self.dim, residual, weight, eps, out)
+
 
 def tp_model(full: MambaModel, rank: int, world: int, group=None, peer_rows: int = 0) -> MambaModel:
     """Builds this rank's tensor-parallel MambaModel from a full one (same device and dtype).

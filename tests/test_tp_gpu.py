@@ -107,6 +107,34 @@ def _peer_worker(rank, world, port, q):
             if peer.timed_out():
                 bad.append((str(dtype), "timeout"))
             del peer
+        # all-reduce fused with residual add + RMSNorm (low-latency protocol, one CTA per row)
+        for dtype in (torch.float32, torch.bfloat16):
+            rows, dim = 5, 2560
+            peer = PeerAllReduce(dist.group.WORLD, dev, dtype, [rows * dim, rows * dim])
+            g = torch.Generator().manual_seed(77)
+            res0 = torch.randn(rows, dim, generator=g)
+            w = torch.rand(dim, generator=g) + 0.5
+            for it in range(3):
+                parts = [torch.randn(rows, dim, generator=torch.Generator().manual_seed(500 + 10 * it + r)).to(dtype)
+                         for r in range(world)]
+                site = it % 2
+                peer.slot(site)[:rows * dim].view(rows, dim).copy_(parts[rank])
+                res = res0.to(dev).contiguous()
+                out = torch.empty(rows, dim, dtype=dtype, device=dev)
+                peer.reduce_add_rmsnorm(site, rows, dim, res, w.to(dev), 1e-5, out)
+                s = parts[0].float()
+                for r in range(1, world):
+                    s = s + parts[r].float()
+                want_res = res0 + s.to(dtype).float()
+                want = want_res * torch.rsqrt((want_res * want_res).mean(-1, keepdim=True) + 1e-5) * w
+                if not torch.equal(res.cpu(), want_res):
+                    bad.append(("addnorm residual", str(dtype), it))
+                tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+                if not torch.allclose(out.float().cpu(), want.to(dtype).float(), rtol=tol, atol=tol):
+                    bad.append(("addnorm out", str(dtype), it))
+            if peer.timed_out():
+                bad.append((str(dtype), "addnorm timeout"))
+            del peer
         q.put((rank, bad))
     except Exception as e:  # pragma: no cover - reported to the parent
         q.put((rank, [repr(e)]))
