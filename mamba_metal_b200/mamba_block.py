@@ -103,7 +103,9 @@ class MambaBlock(nn.Module):
     def step(self, x_token: torch.Tensor, conv_state: torch.Tensor, ssm_state: torch.Tensor, inplace: bool = False,
              defer_out: bool = False):
         """O(1) per-token forward (mamba_block.py:155-198). x_token: (B, 1, d_model).
-        Returns (y (B, 1, d_model), new_conv_state, new_ssm_state)."""
+        Returns (y (B, 1, d_model), new_conv_state, new_ssm_state). With defer_out=True on a
+        tensor-parallel block whose out_proj partial fits the peer all-reduce, y is instead a pending
+        reduction whose add_rmsnorm(residual, weight, eps, dtype) finishes it (MambaModel does this)."""
         E, N, R = self.d_inner, self.d_state, self.dt_rank
         dt_ = self.in_proj.weight.dtype
         if not inplace or conv_state.dtype != torch.float32 or not conv_state.is_contiguous():
