@@ -147,10 +147,21 @@ __global__ void __launch_bounds__(256) conv_tfirst_kernel(const Params p, int ch
     if (p.conv_state && t0 <= p.seqlen - 1 && p.seqlen - 1 < t0 + kE) {
       const int last = p.seqlen - 1 - t0;  // index of t = seqlen-1 in this chunk
       float* cs = p.conv_state + ((long long)b * p.dim + d) * kW;
+      // win[last + k] through a select over the kE possible positions: a run-time index would put the
+      // whole window in local memory for every chunk
+      float sel[kW];
+#pragma unroll
+      for (int k = 0; k < kW; ++k) sel[k] = 0.f;
+#pragma unroll
+      for (int m = 0; m < kE; ++m)
+        if (m == last) {
+#pragma unroll
+          for (int k = 0; k < kW; ++k) sel[k] = win[m + k];
+        }
 #pragma unroll
       for (int k = 0; k < kW; ++k) {
         const int t = p.seqlen - kW + k;
-        cs[k] = t >= 0 ? win[last + k] : 0.f;
+        cs[k] = t >= 0 ? sel[k] : 0.f;
       }
     }
   }
