@@ -80,8 +80,13 @@ struct Params {
 // previous chunk for lane 0, or memory for the warp's first chunk.
 constexpr int kCPT = 4;
 
+#ifndef MM_CONV_MIN_BLOCKS
+#define MM_CONV_MIN_BLOCKS 4  // resident 256-thread CTAs per SM the channel-first kernel is compiled for: 4 (64
+                              // registers) measured ~5% faster than no bound (77 registers); 5 slower
+#endif
+
 template <typename T, bool VEC>
-__global__ void __launch_bounds__(256) conv_tfirst_kernel(const Params p, int chunks_per_row, int warps_per_row) {
+__global__ void __launch_bounds__(256, MM_CONV_MIN_BLOCKS) conv_tfirst_kernel(const Params p, int chunks_per_row, int warps_per_row) {
   const int lane = threadIdx.x & 31;
   const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const long long rows = (long long)p.batch * p.dim;
