@@ -75,12 +75,20 @@ __global__ void __launch_bounds__(128) ssm_step_kernel(const SSMParams p) {
   st_f32(static_cast<T*>(p.y) + b * p.ysb + d, y);
 }
 
-// dstate 16, dim a multiple of 8, 16-byte aligned rows: CTA = 32 channels x 16 batch rows in two
-// groups of 8, 128 threads; thread (dl, q) owns states 4q..4q+3 of channel d0 + dl, so a warp's
+// dstate 16, dim a multiple of 8, 16-byte aligned rows: CTA = 32 channels x kQdGroups groups of kQdRows
+// batch rows, 128 threads; thread (dl, q) owns states 4q..4q+3 of channel d0 + dl, so a warp's
 // 16-byte state accesses are contiguous. At entry the CTA starts cp.async copies of both groups' state
 // rows and dt / x / z row slices (one commit group each; nothing held in registers), loads B | C with
 // plain loads, then computes group 0 while group 1 is still in flight.
-constexpr int kQdCh = 32, kQdRows = 8, kQdGroups = 2, kQdThreads = 128;
+#ifndef MM_SSM_ROWS
+#define MM_SSM_ROWS 4  // batch rows per group in the dstate-16 decode step: 4 (1280 CTAs at batch 64)
+                       // measured 10.1 us vs 12.2 us with 8 at the 2.8b decode shape
+#endif
+#ifndef MM_SSM_GROUPS
+#define MM_SSM_GROUPS 2  // row groups per CTA (copies of later groups overlap earlier groups' compute)
+#endif
+constexpr int kQdCh = 32, kQdRows = MM_SSM_ROWS, kQdGroups = MM_SSM_GROUPS, kQdThreads = 128;
+static_assert((kQdRows * kQdGroups) % (kQdThreads / 32) == 0, "B | C rows are staged four warps at a time");
 
 template <typename T>
 struct QuadSmem {
