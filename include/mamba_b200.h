@@ -159,7 +159,7 @@ int mm_causal_conv1d_fwd(const MMConvArgs* args, mm_stream_t stream);
  *   conv_state[b,d,:] <- [conv_state[b,d,1:], x[b,d]]
  *   out[b,d] = act(bias[d] + sum_k weight[d,k] * conv_state[b,d,k])
  * x, out: (batch, dim) with row strides; conv_state: fp32 (batch, dim, width) contiguous.
- * Replaces mamba_metal/mamba_block.py:171-177.
+ * batch <= 65535. Replaces mamba_metal/mamba_block.py:171-177.
  * ------------------------------------------------------------------------------------------- */
 typedef struct MMConvStepArgs {
   const void* x;

@@ -337,9 +337,10 @@ struct StepParams {
 
 template <typename T>
 __global__ void __launch_bounds__(256) conv_step_kernel(const StepParams p) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long long)p.batch * p.dim) return;
-  const int d = (int)(i % p.dim), b = (int)(i / p.dim);
+  // grid (channel blocks, batch): no per-thread division
+  const int d = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+  if (d >= p.dim) return;
+  const long long i = (long long)b * p.dim + d;
   float4* st = reinterpret_cast<float4*>(p.state + i * kW);
   const float4 s = *st;
   const float xn = ld_f32(static_cast<const T*>(p.x) + b * p.xsb + d);
@@ -397,8 +398,8 @@ extern "C" int mm_causal_conv1d_step(const MMConvStepArgs* a, mm_stream_t stream
   p.xsb = a->x_stride_b; p.osb = a->out_stride_b; p.batch = (int)a->batch; p.dim = (int)a->dim;
   p.silu = a->silu != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const long long n = (long long)p.batch * p.dim;
-  const unsigned blocks = (unsigned)((n + 255) / 256);
+  if (a->batch > 65535 || a->dim > (1 << 30)) return MM_ERR_SHAPE;  // grid.y = batch
+  const dim3 blocks((unsigned)((p.dim + 255) / 256), (unsigned)p.batch);
   if (a->dtype == MM_F32) conv::conv_step_kernel<float><<<blocks, 256, 0, s>>>(p);
   else if (a->dtype == MM_F16) conv::conv_step_kernel<__half><<<blocks, 256, 0, s>>>(p);
   else conv::conv_step_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(p);
