@@ -111,12 +111,15 @@ int mm_selective_scan_fwd(const MMScanArgs* args, void* workspace, size_t worksp
  * start-up. Instead of a caller-provided workspace it uses a scratch buffer of
  * MM_SCAN_NOALLOC_SCRATCH_BYTES that is a static __device__ array of this library: every GPU that loads
  * the library holds it until the process exits. The caller still provides every input and output.
- * Calls whose workspace would exceed the buffer return MM_ERR_TOO_LARGE without launching anything.
- * The first call on a device looks up the buffer's device address (cudaGetSymbolAddress, once per
- * device); make that first call before any stream capture. All calls share the one buffer, so calls
- * that overlap in time on the GPU (other streams, other host threads) race and must be serialised by
- * the caller; each call clears the part of the buffer that must start at zero. No counterpart exists in
- * the reference (its Metal kernel needs no workspace). */
+ * With piece_tiles == 0 the library lengthens the per-warp pieces until the workspace fits the buffer;
+ * calls that cannot fit even so (or whose explicit piece_tiles does not fit) return MM_ERR_TOO_LARGE
+ * without launching anything. The first call on a device (and the first after a device reset, which
+ * reloads the module) looks up the buffer's device address with cudaGetSymbolAddress; make that first
+ * call before any stream capture. All calls share the one buffer, so calls that overlap in time on the
+ * GPU (other streams, other host threads) race and must be serialised by the caller; each call clears
+ * the part of the buffer that must start at zero. A carry wait that reaches its time limit cannot be
+ * observed for these calls (mm_selective_scan_status needs the workspace address, which stays private).
+ * No counterpart exists in the reference (its Metal kernel needs no workspace). */
 #define MM_SCAN_NOALLOC_SCRATCH_BYTES (16u << 20)
 int mm_selective_scan_fwd_noalloc(const MMScanArgs* args, mm_stream_t stream);
 /* Synchronises `stream` and reports MM_OK or MM_ERR_TIMEOUT for the last scan that used

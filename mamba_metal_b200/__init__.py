@@ -2,8 +2,9 @@
 hand-written sm_100a CUDA behind a C-ABI library, under the reference's Python API.
 
 The package directory is ``mamba_metal_b200`` (the hyphenated name cannot be imported in Python).
-Public names mirror mamba_metal/__init__.py:3-20; ``load_mamba_hf`` is not provided (no network or
-checkpoints offline) and ``load_kernel`` (the MLX Metal loader) has no counterpart.
+Public names mirror mamba_metal/__init__.py:3-20. ``load_mamba_hf`` loads a ``state-spaces/mamba-*-hf``
+checkpoint from a local directory or the Hugging Face cache; ``load_kernel`` (the MLX Metal loader) has no
+counterpart.
 """
 
 from mamba_metal_b200.generate import GraphDecoder, generate, generate_fast, generate_ids

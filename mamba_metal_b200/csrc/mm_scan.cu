@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "mm_scan.cuh"
@@ -20,15 +21,21 @@ struct Plan {
   size_t flags_off, agg_off, pre_off;
 };
 
+// Resident warps of the dstate <= 16 kernels on the current device. The SM count is cached per device in
+// atomics: concurrent first calls may both query it, and both store the same value.
 static int resident_warps() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148 * 16;
-  if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148 * MM_SCAN_MIN_BLOCKS * kWarpsPerCta;
+  const bool cacheable = dev >= 0 && dev < 64;
+  if (cacheable) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int v = sms * MM_SCAN_MIN_BLOCKS * kWarpsPerCta;  // resident warps of the dstate <= 16 kernels
-  if (dev >= 0 && dev < 64) cached[dev] = v;
+  const int v = sms * MM_SCAN_MIN_BLOCKS * kWarpsPerCta;
+  if (cacheable) cached[dev].store(v, std::memory_order_relaxed);
   return v;
 }
 
@@ -222,31 +229,78 @@ __device__ __align__(256) unsigned char g_scan_scratch[MM_SCAN_NOALLOC_SCRATCH_B
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
-void* g_scratch_ptr[kMaxDevices] = {nullptr};
+struct ScratchSlot {
+  CUcontext ctx;  // context the address below belongs to
+  void* ptr;
+};
+ScratchSlot g_scratch[kMaxDevices] = {};
 
-// Device address of g_scan_scratch on the current device, looked up once per device. The symbol's
-// name in host code is only a host-side handle; kernels must be given this address.
+// cuCtxGetCurrent through the runtime's driver entry point (no link against libcuda).
+PFN_cuCtxGetCurrent_v4000 ctx_getter() {
+  static const PFN_cuCtxGetCurrent_v4000 fn = []() -> PFN_cuCtxGetCurrent_v4000 {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+  }();
+  return fn;
+}
+
+// Device address of g_scan_scratch on the current device. The symbol's name in host code is only a
+// host-side handle; kernels must be given this address. It is looked up once per device and context:
+// after a device reset the runtime creates a new primary context with the module loaded anew, so the
+// address is looked up again when the current context differs from the cached one.
 int scratch_for_current_device(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MM_ERR_LAUNCH;
+  auto get_ctx = ctx_getter();
+  if (!get_ctx) return MM_ERR_LAUNCH;
+  // Null until the runtime has made the device's primary context current on this thread.
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return MM_ERR_LAUNCH;
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
+  ScratchSlot& slot = g_scratch[dev];
+  if (slot.ptr == nullptr || ctx == nullptr || slot.ctx != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_scan_scratch) != cudaSuccess || p == nullptr) return MM_ERR_LAUNCH;
-    g_scratch_ptr[dev] = p;
+    if (get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) return MM_ERR_LAUNCH;
+    slot.ptr = p;
+    slot.ctx = ctx;
   }
-  *out = g_scratch_ptr[dev];
+  *out = slot.ptr;
   return MM_OK;
+}
+
+// Work plan whose workspace fits the fixed scratch buffer. With piece_tiles == 0 (library's choice) the
+// default plan targets one piece per resident warp; when its workspace (one flag line and two state
+// blocks per warp) does not fit, pieces are lengthened until it does. An explicit piece_tiles is kept.
+int plan_within_scratch(const MMScanArgs* a, MMScanArgs* fitted, size_t* need) {
+  *fitted = *a;
+  int rc = mm_selective_scan_workspace_size(fitted, need);
+  if (rc != MM_OK || *need <= MM_SCAN_NOALLOC_SCRATCH_BYTES || a->piece_tiles > 0) return rc;
+  Plan pl;
+  rc = make_plan(a, &pl);
+  if (rc != MM_OK) return rc;
+  const size_t per_warp = sizeof(unsigned) * kFlagStride + sizeof(float) * (size_t)(2 * pl.NM + 1) * 32;
+  const size_t fixed = 256 + 3 * 256;  // header + alignment slack of the three per-warp arrays
+  const long long max_warps = (long long)((MM_SCAN_NOALLOC_SCRATCH_BYTES - fixed) / per_warp);
+  if (max_warps < 1) return MM_ERR_TOO_LARGE;
+  fitted->piece_tiles = (pl.total_tiles + max_warps - 1) / max_warps;
+  return mm_selective_scan_workspace_size(fitted, need);
 }
 }  // namespace
 
 extern "C" int mm_selective_scan_fwd_noalloc(const MMScanArgs* a, mm_stream_t stream) {
+  if (!a) return MM_ERR_ARG;
+  MMScanArgs fitted;
   size_t need = 0;
-  const int rc = mm_selective_scan_workspace_size(a, &need);
+  const int rc = plan_within_scratch(a, &fitted, &need);
   if (rc != MM_OK) return rc;
   if (need > MM_SCAN_NOALLOC_SCRATCH_BYTES) return MM_ERR_TOO_LARGE;
   void* ws = nullptr;
   const int rs = scratch_for_current_device(&ws);
   if (rs != MM_OK) return rs;
-  return mm_selective_scan_fwd(a, ws, MM_SCAN_NOALLOC_SCRATCH_BYTES, stream);
+  return mm_selective_scan_fwd(&fitted, ws, MM_SCAN_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -8,7 +8,7 @@ has no CPU fallback.
 Contents:
 
 - ``scan_ref``   -- NumPy restatement of the reference's own sequential CPU references for the scan
-  (``experiments/09-features/test_features.py:13-43``, ``experiments/10-fp16/test_fp16.py:139-174``,
+  (``experiments/09-features/test_features.py:13-43``, ``experiments/10-fp16/test_fp16.py:28-55``,
   ``experiments/18-prefill/verify_state_out.py:13-26``, ``experiments/05-pair-scan/pair_scan.py:36-42``),
   the conv1d semantics of ``mamba_metal/mamba_block.py:45-52`` and the decode-step formulas of
   ``mamba_metal/mamba_block.py:155-198``. Pinned against golden vectors produced by running those

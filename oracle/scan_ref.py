@@ -37,7 +37,7 @@ def selective_scan_literal(u, delta, A, B, C, D=None, z=None, delta_softplus=Fal
     """Sequential reference scan, per (batch, channel), in float32.
 
     Restates experiments/09-features/test_features.py:23-43 (y), with the float32 upcast of
-    experiments/10-fp16/test_fp16.py:147-156 and the final state of
+    experiments/10-fp16/test_fp16.py:28-36 and the final state of
     experiments/18-prefill/verify_state_out.py:13-26. Shapes: u, delta, z (batch, dim, seqlen);
     A (dim, dstate); B, C (batch, dstate, seqlen); D (dim,).
     """
@@ -222,7 +222,7 @@ def make_features_inputs(batch, dim, dstate, seqlen, seed=0):
 
 
 def make_fp16_inputs(batch, dim, dstate, seqlen, seed=0):
-    """experiments/10-fp16/test_fp16.py:177-186: u, B, C ~ N(0,1)*0.5, delta ~ U(0.01, 0.1),
+    """experiments/10-fp16/test_fp16.py:58-67: u, B, C ~ N(0,1)*0.5, delta ~ U(0.01, 0.1),
     A ~ -U(0.1, 2), D ~ N(0,1), z ~ N(0,1)."""
     rng = np.random.default_rng(seed)
     u = rng.standard_normal((batch, dim, seqlen)).astype(np.float32) * 0.5
@@ -236,7 +236,7 @@ def make_fp16_inputs(batch, dim, dstate, seqlen, seed=0):
 
 
 def make_chunked_inputs(batch, dim, dstate, seqlen, seed=0):
-    """experiments/07-chunked/selective_scan_chunked.py:114-120 (also 08-benchmark/bench.py:38-48):
+    """experiments/07-chunked/selective_scan_chunked.py:29-35 (also 08-benchmark/bench.py:38-48):
     u ~ N(0,1), delta ~ U(0.01, 0.1), A ~ -U(0.1, 2), B, C ~ N(0,1)."""
     rng = np.random.default_rng(seed)
     u = rng.standard_normal((batch, dim, seqlen)).astype(np.float32)

@@ -10,9 +10,9 @@ where the reference is mounted (it is not needed, and not present, on the GPU bo
 
 Functions used (file:line in the reference):
   experiments/09-features/test_features.py  softplus_safe :13, silu :19, reference :23, make_inputs :46
-  experiments/10-fp16/test_fp16.py           reference_fp32 :147, make_inputs :177
-  experiments/18-prefill/verify_state_out.py reference_h_final :13, main's input draws :39-46
-  experiments/07-chunked/selective_scan_chunked.py selective_scan_ref :14, run_test draws :29-35
+  experiments/10-fp16/test_fp16.py           reference_fp32 :28, make_inputs :58
+  experiments/18-prefill/verify_state_out.py reference_h_final :13, main's input draws :30-36
+  experiments/07-chunked/selective_scan_chunked.py selective_scan_ref :14, run_test draws :30-35
   experiments/05-pair-scan/pair_scan.py      reference :36, main's input draws :56-81
 
 The reference's feature test seeds each case with ``hash(name)`` (test_features.py:60), which is not
@@ -81,7 +81,7 @@ def main(ref_root: Path) -> None:
                                          "shape": [b, d, n, t], "seed": seed,
                                          "note": "non-softplus cases take delta_sp as delta (test_features.py:63-69)"})
 
-    # 2. fp16 mixed precision (test_fp16.py:229-243): fp32 reference on the unrounded fp32 inputs
+    # 2. fp16 mixed precision (test_fp16.py:110-124): fp32 reference on the unrounded fp32 inputs
     for tag, (b, d, n, t), seed in (("T1024", (2, 4, 16, 1024), 0), ("T4096", (1, 2, 16, 4096), 0)):
         u, delta, A, B, C, D, z = fp16["make_inputs"](b, d, n, t, seed)
         arrays = dict(u=u, delta=delta, A=A, B=B, C=C, D=D, z=z)
@@ -90,10 +90,10 @@ def main(ref_root: Path) -> None:
                 continue
             arrays[f"y_{name}"] = fp16["reference_fp32"](u, delta, A, B, C, D=D if use_d else None,
                                                          z=z if use_z else None, delta_softplus=bool(sp))
-        save(f"fp16_{tag}", arrays, {"source": "experiments/10-fp16/test_fp16.py:147-243", "shape": [b, d, n, t],
+        save(f"fp16_{tag}", arrays, {"source": "experiments/10-fp16/test_fp16.py:28-128", "shape": [b, d, n, t],
                                      "seed": seed})
 
-    # 3. final state (verify_state_out.py:38-46): one generator shared across the three shapes
+    # 3. final state (verify_state_out.py:30-36): one generator shared across the three shapes
     rng = np.random.default_rng(0)
     arrays = {}
     for i, (b, d, n, t) in enumerate([(1, 2, 8, 256), (2, 4, 16, 1024), (1, 4, 16, 4096)]):
@@ -104,9 +104,9 @@ def main(ref_root: Path) -> None:
         Cw = rng.standard_normal((b, n, t)).astype(np.float32)
         arrays.update({f"u{i}": u, f"delta{i}": delta, f"A{i}": A, f"B{i}": Bw, f"C{i}": Cw,
                        f"h{i}": state["reference_h_final"](u, delta, A, Bw)})
-    save("state", arrays, {"source": "experiments/18-prefill/verify_state_out.py:13-46", "cases": 3})
+    save("state", arrays, {"source": "experiments/18-prefill/verify_state_out.py:13-49", "cases": 3})
 
-    # 4. chunk boundaries (selective_scan_chunked.py:114-146), seed 0 per case
+    # 4. chunk boundaries (selective_scan_chunked.py:29-61), seed 0 per case
     arrays = {}
     for i, (b, d, n, t) in enumerate([(1, 2, 8, 512), (1, 2, 8, 1024), (1, 2, 8, 1025), (1, 4, 16, 2048)]):
         rng = np.random.default_rng(0)
@@ -117,7 +117,7 @@ def main(ref_root: Path) -> None:
         Cw = rng.standard_normal((b, n, t)).astype(np.float32)
         arrays.update({f"u{i}": u, f"delta{i}": delta, f"A{i}": A, f"B{i}": Bw, f"C{i}": Cw,
                        f"y{i}": chunk["selective_scan_ref"](u, delta, A, Bw, Cw)})
-    save("chunked", arrays, {"source": "experiments/07-chunked/selective_scan_chunked.py:14-146", "cases": 4})
+    save("chunked", arrays, {"source": "experiments/07-chunked/selective_scan_chunked.py:14-61", "cases": 4})
 
     # 5. pair scan known answers (pair_scan.py:56-81)
     rng = np.random.default_rng(0)

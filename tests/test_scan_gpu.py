@@ -60,7 +60,7 @@ def test_fp16_golden(golden_dir, tag):
                                        D=r16["D"] if ud else None, z=r16["z"] if uz else None, delta_softplus=bool(sp))
         assert_close(y, ref, RTOL["float16"], f"fp16 {tag} {name}")
         # ... and against the reference's fp32 golden on the unrounded inputs, as the reference test does
-        # (test_fp16.py:217-220 prints the error with |ref| > 1e-2, "~1e-3 typical"). That error is set by
+        # (test_fp16.py:98-101 prints the error with |ref| > 1e-2, "~1e-3 typical"). That error is set by
         # rounding the inputs to fp16 (2^-11 each), not by the kernel: bound it in absolute terms on the
         # data's scale, and the median relative error at the reference's "typical" level.
         gold = g[f"y_{name}"]

@@ -37,20 +37,23 @@ def _args(u, delta, A, Bm, Cm, D, z, y, state, softplus=True):
     return a
 
 
-@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
-def test_noalloc_matches_workspace_entry_point(dtype):
-    inp = R.make_baseline_inputs(2, 200, 16, 3000, seed=21)
+def _run_both(shape, dtype, seed):
+    """Runs the workspace entry point once and the no-alloc entry point twice in a row on the same
+    inputs; checks both no-alloc calls against the workspace call and returns the inputs (fp32, as the
+    kernel saw them after rounding to `dtype`) with the last no-alloc outputs."""
+    b, d, n, L = shape
+    inp = R.make_baseline_inputs(b, d, n, L, seed=seed)
     t = {k: torch.as_tensor(v).to(DEV, dtype if k in ("u", "delta", "z", "B", "C") else torch.float32)
          for k, v in inp.items()}
     y_ref = torch.empty_like(t["u"])
-    h_ref = torch.empty((2, 200, 16), device=DEV)
+    h_ref = torch.empty((b, d, n), device=DEV)
     selective_scan_into(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"], y_ref, h_ref, True)
     lib = _lib.lib()
     stream = _lib.stream_handle(DEV)
     name = str(dtype).split(".")[-1]
     for call in range(2):  # the shared buffer keeps the previous call's contents: both must be right
         y = torch.full_like(t["u"], float("nan"))
-        h = torch.full((2, 200, 16), float("nan"), device=DEV)
+        h = torch.full((b, d, n), float("nan"), device=DEV)
         a = _args(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"], y, h)
         with torch.cuda.device(DEV):
             rc = lib.mm_selective_scan_fwd_noalloc(ctypes.byref(a), stream)
@@ -58,6 +61,35 @@ def test_noalloc_matches_workspace_entry_point(dtype):
         torch.cuda.synchronize()
         assert_close(y, y_ref, RTOL[name], f"no-alloc call {call} y")
         assert_close(h, h_ref, RTOL["float32"], f"no-alloc call {call} state")
+    return {k: v.float().cpu().numpy() for k, v in t.items()}, y, h
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_noalloc_matches_workspace_entry_point(dtype):
+    x, y, h = _run_both((2, 200, 16, 3000), dtype, seed=21)
+    # and against the sequential oracle on the same (rounded) inputs
+    y_o, h_o = R.selective_scan_vec(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], x["z"],
+                                    delta_softplus=True, return_state=True)
+    assert_close(y, y_o, RTOL[str(dtype).split(".")[-1]], "no-alloc y vs oracle")
+    assert_close(h, h_o, RTOL["float32"], "no-alloc state vs oracle")
+
+
+def test_noalloc_fits_large_state_by_longer_pieces():
+    """dstate 64, bf16, (1, 2048, 4096): the library's default split (one piece per resident warp)
+    would need about 17 MB of workspace, more than the fixed buffer; the no-alloc entry point lengthens
+    the pieces until the workspace fits instead of refusing the call."""
+    a = _lib.MMScanArgs()
+    a.dtype, a.batch, a.dim, a.dstate, a.seqlen = _lib.DTYPE_CODE[torch.bfloat16], 1, 2048, 64, 4096
+    need = ctypes.c_size_t(0)
+    with torch.cuda.device(DEV):
+        assert _lib.lib().mm_selective_scan_workspace_size(ctypes.byref(a), ctypes.byref(need)) == 0
+    assert need.value > _lib.MM_SCAN_NOALLOC_SCRATCH_BYTES
+    x, y, h = _run_both((1, 2048, 64, 4096), torch.bfloat16, seed=5)
+    from oracle.scan_c import selective_scan_c
+
+    y_o, h_o = selective_scan_c(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], x["z"], delta_softplus=True)
+    assert_close(y, y_o, RTOL["bfloat16"], "no-alloc dstate-64 y vs oracle")
+    assert_close(h, h_o, RTOL["float32"], "no-alloc dstate-64 state vs oracle")
 
 
 def test_noalloc_rejects_too_large():
