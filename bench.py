@@ -1,23 +1,27 @@
-"""Benchmark of the selective-scan hot path on 1..8 B200s.
+"""Benchmark of the selective-scan hot path and of configs[3] decode, on 1..8 B200s.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
 
-One step = one selective-scan forward over the configs[1] batch: fp16 u / delta / z / B / C with fp32
-A / D, batch 8, dim 1536, dstate 16, seqlen 4096, D skip, SiLU(z) gate, softplus(delta), final state
-returned. Inputs are seeded synthetic data with the BASELINE distributions (no dataset exists for this
-path). With N > 1 (torchrun, one process per GPU) every rank runs the same per-GPU batch: the scan
-shards by (batch, channel) with no communication, so scaling is weak and the value is the whole-job
-element rate (all ranks' elements / max-over-ranks time).
+Default line (workload `scan`). One step = one selective-scan forward over the configs[1] batch: fp16
+u / delta / z / B / C with fp32 A / D, batch 8, dim 1536, dstate 16, seqlen 4096, D skip, SiLU(z) gate,
+softplus(delta), final state returned. Inputs are seeded synthetic data with the BASELINE distributions
+(no dataset exists for this path). With N > 1 (torchrun, one process per GPU) rank r scans batch rows
+[r*8/N, (r+1)*8/N): the scan shards by (batch, channel) with no communication, the total work is fixed
+(strong scaling), and the value is the whole batch's element rate over the max-over-ranks launch time.
+L2 is flushed before every timed launch (each rank's shard is smaller than L2 at N >= 4).
 
 Printed JSON (rank 0, one line):
-  value       Gelem/s with inputs resident in HBM (CUDA events around K launches, max over ranks)
+  value       Gelem/s with inputs resident in HBM (CUDA events around each launch, max over ranks)
   e2e         the same through the public selective_scan API with pinned host inputs: H2D copies of
               u/delta/z/B/C, the scan, and the D2H read of y and the state inside the timed region
   roofline    algorithmic bytes per launch / average launch time vs the measured HBM copy bandwidth
   cpu_baseline the C restatement of the reference's sequential scan on this host's cores, on a bounded
               sample of the same workload (rank 0, N = 1 only)
+  decode      BASELINE configs[3] (Mamba-2.8b architecture, bf16, batch 64, prompt 2048): greedy decode
+              tok/s through the CUDA-graph step, tensor-parallel over N GPUs, with its own roofline, e2e
+              and clocks
 --impl reference times that CPU scan alone (the reference itself is Python + Metal through MLX and has
-no CPU-runnable build here), on the same metric.
+no CPU-runnable build here), on the same metric and config.
 """
 
 from __future__ import annotations
@@ -165,6 +169,28 @@ def cpu_scan_rate(inp, budget_s=10.0):
                                        f"steps ({elems} elements, {dt:.1f} s), fp32 math on the fp32 inputs")
 
 
+def fma_roofline(elems, dstate, launch_ms, sms=148, clock_ghz=1.965):
+    """Compute floor of the scan on the FMA pipe: 3 FMA-pipe operations per (element, state) -- the decay
+    factor, the state update and the output sum -- at 128 FP32 lanes per SM per clock; reported as the
+    floor time and its ratio to the measured launch time (the FMA-pipe counterpart of the HBM roofline)."""
+    floor_ms = 3 * dstate * elems / (sms * 128 * clock_ghz * 1e9) * 1e3
+    return {"bound": "fma", "ops_per_elem_state": 3, "floor_ms": floor_ms, "frac": floor_ms / launch_ms,
+            "clock_ghz": clock_ghz}
+
+
+def scan_config():
+    """The `config` object of the default line, shared by both arms so that they describe one workload."""
+    return {"workload": "selective_scan configs[1]: fp16 u/delta/z/B/C, fp32 A/D, D skip, SiLU(z), softplus, "
+            "final state", **CFG, "sharding": "batch rows over ranks (strong scaling), no communication",
+            "l2": "L2 flushed (256 MB write) before every timed launch"}
+
+
+def cpu_info(threads):
+    import torch
+
+    return {"cores": threads, "os_cpu_count": os.cpu_count(), "torch_num_threads": torch.get_num_threads()}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -176,18 +202,47 @@ def run_reference(args, rank, world):
         r, threads, sample = cpu_scan_rate(inp, budget_s=max(2.0, 60.0 / max(args.steps, 1)))
         rates.append(r)
     value = statistics.median(rates)
+    elems = CFG["batch"] * CFG["dim"] * CFG["seqlen"]
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "Gelem/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (BASELINE configs[1] "
-            "distributions, seed 0)",
-            "config": {"workload": "selective_scan configs[1] (bounded CPU sample)", **CFG, "fp16_inputs": True},
-            "cpu_baseline": {"value": value, "unit": "Gelem/s", "cores": threads, "kind": "port", "sample": sample},
-            "e2e": {"value": value, "unit": "Gelem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": elems / (value * 1e9) * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (BASELINE configs[1] distributions, seed 0)", "config": scan_config(),
+            "cpu_baseline": {"value": value, "unit": "Gelem/s", **cpu_info(threads), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "Gelem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the C restatement of the reference's sequential CPU scan, all host threads, rank 0 only; "
+                    "ms_per_step is the full configs[1] batch at the measured rate"}
     print(json.dumps(line), flush=True)
 
 
+def shard_rows(world, rank):
+    """Batch rows [b0, b1) of configs[1] that this rank scans (contiguous, equal shares)."""
+    nb = CFG["batch"]
+    if nb % world:
+        raise SystemExit(f"configs[1] has {nb} batch rows: --gpus {world} does not divide them")
+    per = nb // world
+    return rank * per, (rank + 1) * per
+
+
+def e2e_chunks(rows, dim, n_chunks=4):
+    """Splits a (rows, dim) block into n_chunks (row range, channel range) pieces whose (row, channel,
+    time) slices are contiguous: whole rows when there are at least n_chunks rows, else channel ranges
+    (multiples of 32) of single rows."""
+    if rows >= n_chunks:
+        per = rows // n_chunks
+        return [((i * per, (i + 1) * per), (0, dim)) for i in range(n_chunks)]
+    parts = n_chunks // rows
+    step = ((dim + parts - 1) // parts + 31) // 32 * 32
+    out = []
+    for r in range(rows):
+        for c0 in range(0, dim, step):
+            out.append(((r, r + 1), (c0, min(dim, c0 + step))))
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
-    """configs[1] selective scan (the default workload)."""
+    """configs[1] selective scan (the default workload). Rank r scans batch rows [r*8/N, (r+1)*8/N);
+    value = all ranks' elements / max-over-ranks mean launch time (strong scaling)."""
     import torch
     import torch.distributed as dist
 
@@ -196,71 +251,79 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    sync_all, max_over_ranks = _dist_tools(dev, world)
+    b0, b1 = shard_rows(world, rank)
     inp = make_inputs(seed=0)
-    h16 = {k: torch.from_numpy(inp[k]).to(torch.float16).pin_memory() for k in ("u", "delta", "z", "B", "C")}
+    h16 = {k: torch.from_numpy(inp[k][b0:b1]).to(torch.float16).pin_memory() for k in ("u", "delta", "z", "B", "C")}
     h32 = {k: torch.from_numpy(inp[k]).pin_memory() for k in ("A", "D")}
     d = {k: v.to(dev, non_blocking=True) for k, v in {**h16, **h32}.items()}
-    b, dm, n, L = CFG["batch"], CFG["dim"], CFG["dstate"], CFG["seqlen"]
+    b, dm, n, L = b1 - b0, CFG["dim"], CFG["dstate"], CFG["seqlen"]
     y = torch.empty((b, dm, L), dtype=torch.float16, device=dev)
     state = torch.empty((b, dm, n), dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
     stream = torch.cuda.current_stream(dev)
 
     def step():
         selective_scan_into(d["u"], d["delta"], d["A"], d["B"], d["C"], d["D"], d["z"], y, state, True)
 
-    def sync_all():
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     for _ in range(args.warmup):
+        flush.zero_()
         step()
     sync_all()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
     with ClockSampler(_nvml_index(local_rank)) as clk:
         sync_all()
-        t_start = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
-        t_start.record(stream)
         torch.cuda.nvtx.range_push("timed")  # ncu --nvtx --nvtx-include "timed/" selects these launches
         for k in range(args.steps):
+            flush.zero_()
             ev[2 * k].record(stream)
             step()
             ev[2 * k + 1].record(stream)
         torch.cuda.nvtx.range_pop()
-        t_end.record(stream)
         sync_all()
-    total_ms = max_over_ranks(t_start.elapsed_time(t_end))
     launch_ms = max_over_ranks(statistics.mean(ev[2 * k].elapsed_time(ev[2 * k + 1]) for k in range(args.steps)))
     elems = b * dm * L
-    ms_per_step = total_ms / args.steps
-    value = world * elems / (ms_per_step * 1e-3) / 1e9
+    value = world * elems / (launch_ms * 1e-3) / 1e9
+
+    # the same workload with a trained-checkpoint-like A (A = -exp(A_log), A_log ~ U(log 0.5, log 16) per
+    # (channel, state)): the kernel's general-A path, one exp2 per state and step
+    A_struct = d["A"]
+    gA = torch.Generator().manual_seed(7)
+    d["A"] = (-torch.exp(torch.empty((dm, n)).uniform_(np.log(0.5), np.log(16.0), generator=gA))).to(dev)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    sync_all()
+    for k in range(args.steps):
+        flush.zero_()
+        ev[2 * k].record(stream)
+        step()
+        ev[2 * k + 1].record(stream)
+    sync_all()
+    general_ms = max_over_ranks(statistics.mean(ev[2 * k].elapsed_time(ev[2 * k + 1]) for k in range(args.steps)))
+    d["A"] = A_struct
+    del flush
 
     if args.no_extras:
         if rank == 0:
-            print(json.dumps({"metric": METRIC, "value": world * b * dm * L / (total_ms / args.steps * 1e-3) / 1e9,
-                              "unit": "Gelem/s", "ms_per_step": total_ms / args.steps, "launch_ms": launch_ms,
+            print(json.dumps({"metric": METRIC, "value": value, "unit": "Gelem/s", "ms_per_step": launch_ms,
                               "n_gpus": world, "note": "--no-extras: device loop only"}), flush=True)
         return
 
-    # e2e: public API, pinned host inputs, copies inside the timed region. Each step's batch goes in
-    # E2E_CHUNKS row chunks through three streams (upload, scan, download) so the H2D copy of one chunk,
-    # the scan of the previous one and the D2H copy of the one before overlap (PCIe is full duplex);
-    # device buffers alternate between two sets by step parity, ordered by events.
-    E2E_CHUNKS = 4
-    rows = b // E2E_CHUNKS
+    # e2e: public API, pinned host inputs, copies inside the timed region. Each step's shard goes in
+    # four chunks through three streams (upload, scan, download) so the H2D copy of one chunk, the scan
+    # of the previous one and the D2H copy of the one before overlap (PCIe is full duplex); device
+    # buffers alternate between two sets by step parity, ordered by events.
+    chunks = e2e_chunks(b, dm)
     s_in, s_cmp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
-    bufs = [[{k: torch.empty((rows,) + tuple(v.shape[1:]), dtype=v.dtype, device=dev) for k, v in h16.items()}
-             for _ in range(E2E_CHUNKS)] for _ in range(2)]
-    freed = [[torch.cuda.Event() for _ in range(E2E_CHUNKS)] for _ in range(2)]
+
+    def chunk_views(src, ch):
+        (r0, r1), (c0, c1) = ch
+        return {k: (v[r0:r1] if k in ("B", "C") else v[r0:r1, c0:c1]) for k, v in src.items()}
+
+    bufs = [[{k: torch.empty_like(v, device=dev) for k, v in chunk_views(h16, ch).items()} for ch in chunks]
+            for _ in range(2)]
+    freed = [[torch.cuda.Event() for _ in chunks] for _ in range(2)]
     y_host = torch.empty((b, dm, L), dtype=torch.float16).pin_memory()
     s_host = torch.empty((b, dm, n), dtype=torch.float32).pin_memory()
     step_no = [0]
@@ -268,25 +331,26 @@ def run_ours(args, rank, world, local_rank):
     def e2e_step():
         par = step_no[0] & 1
         step_no[0] += 1
-        for c in range(E2E_CHUNKS):
-            sl = slice(c * rows, (c + 1) * rows)
-            dd = bufs[par][c]
+        for ci, ch in enumerate(chunks):
+            (r0, r1), (c0, c1) = ch
+            dd = bufs[par][ci]
+            src = chunk_views(h16, ch)
             loaded, scanned = torch.cuda.Event(), torch.cuda.Event()
             with torch.cuda.stream(s_in):
-                s_in.wait_event(freed[par][c])  # the scan two steps ago has finished reading this set
-                for k, v in h16.items():
-                    dd[k].copy_(v[sl], non_blocking=True)
+                s_in.wait_event(freed[par][ci])  # the scan two steps ago has finished reading this set
+                for k, v in src.items():
+                    dd[k].copy_(v, non_blocking=True)
                 loaded.record(s_in)
             with torch.cuda.stream(s_cmp):
                 s_cmp.wait_event(loaded)
-                yy, hh = selective_scan(dd["u"], dd["delta"], d["A"], dd["B"], dd["C"], D=d["D"], z=dd["z"],
-                                        delta_softplus=True, return_state=True)
-                freed[par][c].record(s_cmp)
+                yy, hh = selective_scan(dd["u"], dd["delta"], d["A"][c0:c1], dd["B"], dd["C"], D=d["D"][c0:c1],
+                                        z=dd["z"], delta_softplus=True, return_state=True)
+                freed[par][ci].record(s_cmp)
                 scanned.record(s_cmp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(scanned)
-                y_host[sl].copy_(yy, non_blocking=True)
-                s_host[sl].copy_(hh, non_blocking=True)
+                y_host[r0:r1, c0:c1].copy_(yy, non_blocking=True)
+                s_host[r0:r1, c0:c1].copy_(hh, non_blocking=True)
                 yy.record_stream(s_out)
                 hh.record_stream(s_out)
 
@@ -303,8 +367,11 @@ def run_ours(args, rank, world, local_rank):
     e1.record(stream)
     sync_all()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
-    h2d = sum(v.numel() * v.element_size() for v in h16.values())
+    h2d = sum(sum(v.numel() * v.element_size() for v in chunk_views(h16, ch).values()) for ch in chunks)
     d2h = y_host.numel() * 2 + s_host.numel() * 4
+    del bufs, y_host, s_host
+
+    decode = None if args.no_decode else decode_measure(args, rank, world, local_rank)
 
     if rank != 0:
         return
@@ -314,23 +381,27 @@ def run_ours(args, rank, world, local_rank):
     cpu = None
     if world == 1:
         rate, threads, sample = cpu_scan_rate(inp)
-        cpu = {"value": rate, "unit": "Gelem/s", "cores": threads, "kind": "port", "sample": sample}
+        cpu = {"value": rate, "unit": "Gelem/s", **cpu_info(threads), "kind": "port", "sample": sample}
     line = {
         "metric": METRIC, "value": value, "unit": "Gelem/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": launch_ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16 in / f32 math", "data": "synthetic (BASELINE configs[1] distributions, "
         "seed 0)",
-        "config": {"workload": "selective_scan configs[1]: fp16 u/delta/z/B/C, fp32 A/D, D skip, SiLU(z), softplus, "
-                   "final state", **CFG, "per_gpu": True, "l2": "inputs larger than L2 (400 MB per step vs 126 MB)"},
+        "config": scan_config(),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": load_traffic(), "peak_kind": peak_kind, "algorithmic_bytes": nbytes,
-                     "launch_ms": launch_ms},
+                     "traffic": load_traffic() if world == 1 else None, "peak_kind": peak_kind,
+                     "algorithmic_bytes": nbytes, "launch_ms": launch_ms, "rows_per_gpu": b},
+        "compute_roofline": fma_roofline(b * dm * L, n, launch_ms),
+        "general_A": {"value": world * elems / (general_ms * 1e-3) / 1e9, "unit": "Gelem/s", "launch_ms": general_ms,
+                      "roofline_frac": nbytes / (general_ms * 1e-3) / 1e9 / peak,
+                      "A": "-exp(U(log 0.5, log 16)) per (channel, state): general-A path"},
         "cpu_baseline": cpu,
         "e2e": {"value": world * elems / (e2e_ms * 1e-3) / 1e9, "unit": "Gelem/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "gpu_launches": args.steps * E2E_CHUNKS,
-                "pipeline": f"{E2E_CHUNKS} batch chunks per step over upload / scan / download streams"},
-        "gpu_launches": args.steps,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "gpu_launches": args.steps * len(chunks),
+                "pipeline": f"{len(chunks)} chunks per step over upload / scan / download streams"},
+        "gpu_launches": args.steps + (decode["gpu_launches"] if decode else 0),
         "clocks": clk.summary(),
+        "decode": decode,
     }
     print(json.dumps(line), flush=True)
 
@@ -536,11 +607,13 @@ def decode_bytes_per_step(world):
     return c["n_layer"] * (per_layer_w + state) / world + 2 * V * dm
 
 
-def run_decode(args, rank, world, local_rank):
+def decode_measure(args, rank, world, local_rank):
     """Mamba-2.8b architecture (64 layers, d_model 2560, d_inner 5120, N 16, dt_rank 160,
     vocab 50280), random init (seed 0), bf16 weights with fp32 state, batch 64, 2,048-token prompts of
     uniform random ids, parallel prefill, then greedy decode with the CUDA-graph step; tensor-parallel over
-    d_inner at N > 1 (two fp32 all-reduces per layer). One step = one token for all 64 sequences."""
+    d_inner at N > 1 (the x_proj and out_proj partial sums all-reduced over NVLink by this library's peer
+    kernels). One step = one token for all 64 sequences. Every rank runs it; returns the `decode` object
+    (meaningful on rank 0)."""
     import torch
 
     from mamba_metal_b200 import GraphDecoder, MambaConfig, MambaModel, generate_ids, init_weights_
@@ -564,21 +637,21 @@ def run_decode(args, rank, world, local_rank):
         logits, conv, ssm = model.prefill(ids, last_only=True)
         first = torch.argmax(logits[:, -1], dim=-1)
         dec = GraphDecoder(model, conv, ssm, first)
-        for _ in range(args.warmup):
+        for _ in range(max(3, args.warmup)):
             dec.step()
         stream = torch.cuda.current_stream(dev)
         with ClockSampler(_nvml_index(local_rank)) as clk:
             sync_all()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            torch.cuda.nvtx.range_push("timed")  # ncu --nvtx --nvtx-include "timed/" selects these launches
+            torch.cuda.nvtx.range_push("timed_decode")
             for _ in range(args.steps):
                 dec.step()
             torch.cuda.nvtx.range_pop()
             e1.record(stream)
             sync_all()
         ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
-        del dec
+        del dec, conv, ssm, logits
         # e2e: prompt ids from pinned host memory, prefill + new_tokens greedy steps, ids read back
         n_new = c["new_tokens"]
         e2e_ms = None
@@ -592,29 +665,135 @@ def run_decode(args, rank, world, local_rank):
             e3.record(stream)
             sync_all()
             e2e_ms = max_over_ranks(e2.elapsed_time(e3))
-    if rank != 0:
-        return
+    del model
+    torch.cuda.empty_cache()
     peak, kind = load_peaks()
     nbytes = decode_bytes_per_step(world)
     ach = nbytes / (ms * 1e-3) / 1e9
-    print(json.dumps({
-        "metric": METRIC, "value": c["batch"] / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16 weights / fp32 state", "data": "synthetic (uniform random prompt ids, "
-        "random-init weights, seed 0)",
+    # libmamba_b200 kernels per step: conv step, SSM step and residual-norm per layer (under tensor
+    # parallelism: conv step, SSM step, the x_proj all-reduce and the out_proj all-reduce fused with the
+    # residual-norm), plus the first norm
+    launches = args.steps * ((4 if world > 1 else 3) * c["n_layer"] + 1)
+    return {
+        "metric": "Mamba-2.8b decode tok/s", "value": c["batch"] / (ms * 1e-3), "unit": "tok/s",
+        "ms_per_step": ms, "steps": args.steps, "scaling": "strong", "dtype": "bf16 weights / fp32 state",
         "config": {"workload": "decode configs[3]: Mamba-2.8b architecture, batch 64, prompt 2048, greedy, CUDA graph",
                    **{k: c[k] for k in ("d_model", "n_layer", "batch", "prompt")}, "parallelism": f"tp{world}"},
         "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                     "traffic": None, "peak_kind": kind, "algorithmic_bytes": nbytes},
+                     "traffic": None, "peak_kind": kind, "algorithmic_bytes_per_gpu": nbytes},
         "e2e": None if e2e_ms is None else {
             "value": c["batch"] * n_new / (e2e_ms * 1e-3), "unit": "tok/s", "ms": e2e_ms,
             "h2d_bytes_per_step": ids_host.numel() * 8 / n_new, "d2h_bytes_per_step": c["batch"] * 8,
-            "note": "prompt H2D + prefill + 256 greedy steps + ids D2H, per generated token"},
-        # libmamba_b200 kernels per step: conv step, SSM step and residual-norm per layer (under tensor
-        # parallelism: conv step, SSM step, the x_proj all-reduce and the out_proj all-reduce fused with
-        # the residual-norm), plus the first norm
-        "gpu_launches": args.steps * ((4 if world > 1 else 3) * c["n_layer"] + 1), "clocks": clk.summary()}),
-          flush=True)
+            "note": f"prompt H2D + prefill + {n_new} greedy steps + ids D2H, per generated token"},
+        "gpu_launches": launches, "clocks": clk.summary()}
+
+
+def run_decode(args, rank, world, local_rank):
+    """configs[3] decode alone, as its own JSON line."""
+    d = decode_measure(args, rank, world, local_rank)
+    if rank != 0:
+        return
+    print(json.dumps({"metric": METRIC, "n_gpus": world, "warmup": args.warmup, "higher_is_better": True,
+                      "vs_baseline": None, "data": "synthetic (uniform random prompt ids, random-init weights, seed 0)",
+                      **{k: v for k, v in d.items() if k != "metric"}}), flush=True)
+
+
+CFG2 = dict(d_model=768, n_layer=24, vocab_size=50280, d_state=16, d_conv=4, expand=2, dt_rank=48, prompt=5601,
+            new_tokens=50)
+
+
+def scan_stats_during(fn):
+    """Runs fn() with every selective scan of the model blocks followed by a read of its statistics
+    (mm_selective_scan_stats); returns (fn's result, summed [spins, look-back hops, recomputed warp steps,
+    pieces], total warp steps). Diagnostics only: each read synchronises the stream."""
+    import ctypes
+
+    import mamba_metal_b200.mamba_block as mb
+    from mamba_metal_b200 import _lib
+
+    orig = mb.selective_scan_into
+    tot = [0, 0, 0, 0]
+    warp_steps = [0]
+
+    def wrapped(u, delta, A, B, C, D, z, y, state_out, delta_softplus, **kw):
+        ws = orig(u, delta, A, B, C, D, z, y, state_out, delta_softplus, **kw)
+        out = (ctypes.c_ulonglong * 4)()
+        _lib.check(_lib.lib().mm_selective_scan_stats(ws.data_ptr(), out, _lib.stream_handle(u.device)),
+                   "mm_selective_scan_stats")
+        for i in range(4):
+            tot[i] += out[i]
+        b, d, L = u.shape
+        warp_steps[0] += b * ((d + 31) // 32) * L
+        return ws
+
+    mb.selective_scan_into = wrapped
+    try:
+        res = fn()
+    finally:
+        mb.selective_scan_into = orig
+    return res, tot, warp_steps[0]
+
+
+def run_prefill(args, rank, world, local_rank):
+    """configs[2] end to end (Mamba-130m architecture, fp32, random init seed 0, one 5,601-token prompt:
+    prompt H2D, parallel prefill, 50 greedy tokens through the CUDA-graph step, tokens D2H) -- the
+    reference's README quotes 0.88 s for this on an M4 Max (context, not a target) -- and the prefill
+    scans' carry statistics (look-back hops, recomputed steps) for the configs[2] and configs[3] prefill
+    shapes with the models' own delta. One GPU; rank 0 only."""
+    import torch
+
+    from mamba_metal_b200 import MambaConfig, MambaModel, generate_ids, init_weights_
+
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    c = CFG2
+    cfg2 = MambaConfig(**{k: c[k] for k in ("d_model", "n_layer", "vocab_size", "d_state", "d_conv", "expand",
+                                           "dt_rank")})
+    out = {}
+    with torch.no_grad():
+        m2 = init_weights_(MambaModel(cfg2, device=dev), seed=0)
+        ids_host = torch.randint(0, c["vocab_size"], (1, c["prompt"]),
+                                 generator=torch.Generator().manual_seed(0)).pin_memory()
+        toks_host = torch.empty((1, c["new_tokens"]), dtype=torch.long).pin_memory()
+        stream = torch.cuda.current_stream(dev)
+        times = []
+        for i in range(max(1, args.warmup) + max(1, min(args.steps, 5))):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(dev)
+            e0.record(stream)
+            toks = generate_ids(m2, ids_host.to(dev, non_blocking=True), c["new_tokens"])
+            toks_host.copy_(toks, non_blocking=True)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            if i >= max(1, args.warmup):
+                times.append(e0.elapsed_time(e1))
+        _, st, ws = scan_stats_during(lambda: m2.prefill(ids_host.to(dev), last_only=True))
+        out["config2"] = {"e2e_ms": statistics.median(times), "runs": len(times),
+                          "reference_published_s": 0.88, "reference_hw": "M4 Max (README.md:46-51)",
+                          "scan_recomputed_frac": st[2] / ws, "lookback_hops": st[1], "pieces": st[3]}
+        del m2
+        torch.cuda.empty_cache()
+        d = DECODE
+        cfg3 = MambaConfig(d_model=d["d_model"], n_layer=d["n_layer"], vocab_size=d["vocab_size"],
+                           d_state=d["d_state"], d_conv=d["d_conv"], expand=d["expand"], dt_rank=d["dt_rank"])
+        m3 = init_weights_(MambaModel(cfg3, dtype=torch.bfloat16, device=dev), seed=0)
+        ids3 = torch.randint(0, d["vocab_size"], (d["batch"], d["prompt"]), generator=torch.Generator().manual_seed(0))
+        ids3 = ids3.to(dev)
+        m3.prefill(ids3, last_only=True)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        m3.prefill(ids3, last_only=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        _, st3, ws3 = scan_stats_during(lambda: m3.prefill(ids3, last_only=True))
+        out["config3_prefill"] = {"ms": e0.elapsed_time(e1), "tok_s": d["batch"] * d["prompt"] / (e0.elapsed_time(e1) * 1e-3),
+                                  "scan_recomputed_frac": st3[2] / ws3, "lookback_hops": st3[1], "pieces": st3[3]}
+    print(json.dumps({"metric": "configs[2] prefill + 50 greedy tokens, end to end", "value": out["config2"]["e2e_ms"],
+                      "unit": "ms", "higher_is_better": False, "n_gpus": 1,
+                      "data": "synthetic (uniform random prompt ids, random-init weights, seed 0)", **out}), flush=True)
 
 
 def main():
@@ -624,10 +803,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="device loop only: no e2e arm, no CPU baseline")
-    ap.add_argument("--workload", choices=["scan", "conv", "decode", "long"], default="scan",
+    ap.add_argument("--no-decode", action="store_true", help="scan workload: leave out the configs[3] decode object")
+    ap.add_argument("--workload", choices=["scan", "conv", "decode", "long", "prefill"], default="scan",
                     help="scan: configs[1] selective scan (default, the headline); conv: configs[1] causal conv1d; "
                          "decode: configs[3] Mamba-2.8b-architecture batch-64 decode, tensor-parallel at N > 1; "
-                         "long: configs[4] long-context scan, channel-sharded at N > 1")
+                         "long: configs[4] long-context scan, channel-sharded at N > 1; prefill: configs[2] prefill + "
+                         "50 tokens end to end, and the prefill scans' carry statistics for configs[2] / configs[3]")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -645,7 +826,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        {"scan": run_ours, "conv": run_conv, "decode": run_decode, "long": run_long}[args.workload](
+        {"scan": run_ours, "conv": run_conv, "decode": run_decode, "long": run_long, "prefill": run_prefill}[
+            args.workload](
             args, rank, world, local_rank)
     finally:
         if world > 1:

@@ -279,6 +279,11 @@ typedef struct MMPeerAddNormArgs {
 
 int mm_peer_allreduce_add_rmsnorm(const MMPeerAddNormArgs* args, mm_stream_t stream);
 
+/* Self-check of the kernels' device math: y_poly[i] = 2^x[i] from the FMA-pipe polynomial the scan uses for
+ * part of its exponentials with general A, y_mufu[i] = the hardware ex2.approx of x[i]; n floats each,
+ * device pointers. Test and diagnostics use only; no counterpart in the reference. */
+int mm_exp2_check(const float* x, float* y_poly, float* y_mufu, int64_t n, mm_stream_t stream);
+
 /* Library version string (static storage). */
 const char* mm_version(void);
 

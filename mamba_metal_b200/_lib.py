@@ -104,6 +104,7 @@ _SIGNATURES = {
     "mm_add_rmsnorm": ([ctypes.POINTER(MMAddNormArgs), _p], ctypes.c_int),
     "mm_peer_allreduce": ([ctypes.POINTER(MMPeerReduceArgs), _p], ctypes.c_int),
     "mm_peer_allreduce_add_rmsnorm": ([ctypes.POINTER(MMPeerAddNormArgs), _p], ctypes.c_int),
+    "mm_exp2_check": ([_p, _p, _p, _i64, _p], ctypes.c_int),
     "mm_version": ([], ctypes.c_char_p),
 }
 

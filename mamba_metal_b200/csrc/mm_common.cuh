@@ -34,6 +34,19 @@ MM_DEV float rcp(float x) {
 }
 
 // ---- Packed fp32 pairs (Blackwell f32x2 ALU ops: one issue slot for two lanes of math) ---------
+// With MM_F2_SCALAR defined the same helpers are plain scalar C++ (two independent float operations),
+// leaving instruction selection and scheduling entirely to the compiler.
+#ifdef MM_F2_SCALAR
+struct f2_t {
+  float x, y;
+};
+MM_DEV f2_t f2_pack(float lo, float hi) { return f2_t{lo, hi}; }
+MM_DEV float2 f2_unpack(f2_t v) { return make_float2(v.x, v.y); }
+MM_DEV f2_t f2_fma(f2_t a, f2_t b, f2_t c) { return f2_t{fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y)}; }
+MM_DEV f2_t f2_mul(f2_t a, f2_t b) { return f2_t{a.x * b.x, a.y * b.y}; }
+MM_DEV f2_t f2_add(f2_t a, f2_t b) { return f2_t{a.x + b.x, a.y + b.y}; }
+MM_DEV f2_t f2_sub(f2_t a, f2_t b) { return f2_t{a.x - b.x, a.y - b.y}; }
+#else
 typedef unsigned long long f2_t;
 
 MM_DEV f2_t f2_pack(float lo, float hi) {
@@ -56,6 +69,43 @@ MM_DEV f2_t f2_mul(f2_t a, f2_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+MM_DEV f2_t f2_add(f2_t a, f2_t b) {
+  f2_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+MM_DEV f2_t f2_sub(f2_t a, f2_t b) {
+  f2_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+#endif
+
+// ---- 2^x on the FMA pipe, for a pair of arguments ----------------------------------------------
+// Cody-Waite style range reduction x = j + f with j = rint(x) and |f| <= 1/2 (j from the "add 1.5 * 2^23"
+// rounding trick: the low bits of t = x + 1.5 * 2^23 hold j, and (t - 1.5 * 2^23) is j exactly), then
+// 2^f from a degree-5 polynomial whose coefficients are the minimax (Remez exchange, relative error) fit
+// of 2^f on [-1/2, 1/2], rounded to float (csrc/exp2_poly.py reproduces them), and 2^j applied by adding
+// j to the exponent field. Relative error below 2.2e-7 (1.8 ulp) for x in [-125, 126]; arguments are
+// clamped to that range (2^-125 stands in for smaller results). Used to move part of the scan's
+// exponentials off the MUFU pipe, which runs at an eighth of the FMA pipe's rate.
+MM_DEV f2_t exp2_poly2(f2_t x2) {
+  const float2 xs = f2_unpack(x2);
+  const f2_t x = f2_pack(fminf(fmaxf(xs.x, -125.0f), 126.0f), fminf(fmaxf(xs.y, -125.0f), 126.0f));
+  const float kShift = 12582912.0f;  // 1.5 * 2^23
+  const f2_t t = f2_add(x, f2_pack(kShift, kShift));
+  const f2_t f = f2_sub(x, f2_sub(t, f2_pack(kShift, kShift)));
+  f2_t p = f2_pack(1.3276472e-3f, 1.3276472e-3f);
+  p = f2_fma(p, f, f2_pack(9.6755410e-3f, 9.6755410e-3f));
+  p = f2_fma(p, f, f2_pack(5.5507131e-2f, 5.5507131e-2f));
+  p = f2_fma(p, f, f2_pack(2.4022120e-1f, 2.4022120e-1f));
+  p = f2_fma(p, f, f2_pack(6.9314694e-1f, 6.9314694e-1f));
+  p = f2_fma(p, f, f2_pack(1.0000001f, 1.0000001f));
+  const float2 ts = f2_unpack(t);
+  const float2 ps = f2_unpack(p);
+  return f2_pack(__int_as_float(__float_as_int(ps.x) + (__float_as_int(ts.x) << 23)),
+                 __int_as_float(__float_as_int(ps.y) + (__float_as_int(ts.y) << 23)));
+}
 
 // ---- Softplus in the log2 domain --------------------------------------------------------------
 // Returns softplus(x) * log2(e) = log2(1 + e) with e = 2^(x*log2e), and the reference's cutoff
@@ -69,6 +119,21 @@ MM_DEV float softplus_log2(float x) {
   const float ser = e * kLog2e * fmaf(e, fmaf(e, 0.33333334f, -0.5f), 1.0f);
   const float r = (e < 0.015625f) ? ser : l;
   return (x <= 20.0f) ? r : y;
+}
+
+// softplus_log2 of a pair of arguments, with the float arithmetic in packed f32x2 operations.
+MM_DEV f2_t softplus_log2_2(f2_t x2) {
+  const f2_t y = f2_mul(x2, f2_pack(kLog2e, kLog2e));
+  const float2 ys = f2_unpack(y);
+  const f2_t e = f2_pack(ex2(ys.x), ex2(ys.y));
+  const float2 ope = f2_unpack(f2_add(e, f2_pack(1.0f, 1.0f)));
+  const f2_t ser = f2_mul(f2_mul(e, f2_pack(kLog2e, kLog2e)),
+                          f2_fma(e, f2_fma(e, f2_pack(0.33333334f, 0.33333334f), f2_pack(-0.5f, -0.5f)),
+                                 f2_pack(1.0f, 1.0f)));
+  const float2 es = f2_unpack(e), ss = f2_unpack(ser), xs = f2_unpack(x2);
+  const float r0 = (es.x < 0.015625f) ? ss.x : lg2(ope.x);
+  const float r1 = (es.y < 0.015625f) ? ss.y : lg2(ope.y);
+  return f2_pack((xs.x <= 20.0f) ? r0 : ys.x, (xs.y <= 20.0f) ? r1 : ys.y);
 }
 
 // SiLU(z) = z / (1 + exp(-z)) (reference formula, selective_scan_chunked.metal:141-144).

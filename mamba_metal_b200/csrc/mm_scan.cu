@@ -98,6 +98,14 @@ static int make_plan(const MMScanArgs* a, Plan* pl) {
     const long long min_tiles = std::max<long long>(1, (8 * kHeadSteps) / pl->TT);
     const long long want = resident_warps();
     tpw = std::max<long long>(min_tiles, (pl->total_tiles + want - 1) / want);
+    // With at least as many (batch, channel group) rows as warp slots, whole rows per warp need no carry
+    // hand-off at all (no look-back, no recompute, whose length grows as the decay slows); take them when
+    // the longest warp's work grows by at most 1/8 over the split plan.
+    const long long rows = (long long)a->batch * pl->groups_per_batch;
+    if (rows >= want) {
+      const long long whole = ((rows + want - 1) / want) * pl->tiles_per_row;
+      if (8 * whole <= 9 * tpw) tpw = whole;
+    }
   }
   tpw = std::max<long long>(1, std::min<long long>(tpw, std::max<long long>(1, pl->total_tiles)));
   pl->tiles_per_warp = (int)tpw;

@@ -34,6 +34,9 @@ namespace scan {
 #ifndef MM_SCAN_SUBTILE
 #define MM_SCAN_SUBTILE 4  // timesteps of one pass over the state pairs in the recurrence
 #endif
+#ifndef MM_SCAN_POLY_EIGHTHS
+#define MM_SCAN_POLY_EIGHTHS 3  // general A: eighths of the state pairs whose exp2 runs on the FMA pipe
+#endif
 #ifndef MM_SCAN_MIN_BLOCKS
 #define MM_SCAN_MIN_BLOCKS 3  // resident 4-warp CTAs per SM the dstate <= 16 kernels are compiled for: 3 (168
                               // registers) measured 9% faster than 4 (128, with spills) and 3% faster than 2
@@ -225,61 +228,125 @@ MM_DEV void convert_bc(WarpSmem<T, NM>& sm, int slot, int lane) {
   }
 }
 
+// Scaled state. With s_t = delta2_t * u_t (delta2 = delta * log2(e), B staged as B * ln2 so that
+// s_t * B' = delta_t * u_t * B_t) the recurrence h_t = a_t h_{t-1} + s_t B'_t is carried as
+// g_t = h_t / s_t:  g_t = (a_t * s_{t-1} / s_t) g_{t-1} + B'_t,  y_t = s_t * sum_n C_n g_n + D u_t.
+// Per (step, state) that is one decay factor (a multiply in the chain c_n = rho r^(n+1) with
+// rho = s_{t-1} / s_t, or one exp2 and a multiply for general A), one FMA for g and one for y: the
+// s_t * B_t product of the plain form is gone. s_t is kept at least 2^-64 in magnitude (its sign kept),
+// which changes the input term of a step with s_t = 0 by at most 2^-64 * |B|. The reciprocal of s_t shares
+// one MUFU rcp with SiLU's: q = 1 / (s (1 + e^-z)) gives both 1 / s = (1 + e^-z) q and 1 / (1 + e^-z) = s q.
+// `s_prev` carries s_{t-1} across tiles (1 at the start of a range, where g = h).
+constexpr float kMinScale = 5.421010862e-20f;  // 2^-64: smallest |s_t| used as a scale
+constexpr float kMaxExpZ = 1.8446744e19f;      // 2^64: clamp of e^-z (SiLU of z < -44 is then ~0 either way)
+
 // Runs the recurrence over one half tile (HT steps, one 16-byte vector per row) at step offset kb of the
-// staged tile. WY: compute y. ST: A has the S4D-real structure.
-// Phase 1 computes every step's scalars (softplus(delta), exp(delta*A[0]), delta*u, D*u, SiLU(z)) --
+// staged tile. WY: compute y. ST: A has the S4D-real structure. Phase 1 computes every step's scalars
+// (softplus, exp(delta*A[0]), s, rho, SiLU gate, D*u) with packed operations over pairs of steps --
 // independent across steps, so their MUFU latencies overlap. Phase 2 runs in sub-tiles of SK steps with
-// the state pairs in the outer loop: for a fixed pair the h update is the only dependency from one step
-// to the next; the decay powers, the B products and the y partial sums of the SK steps are independent.
+// the state pairs in the outer loop: for a fixed pair the g update is the only dependency from one step
+// to the next; the decay chains and the y partial sums of the SK steps are independent. Phase 2 runs
+// unpredicated: steps past the end of the range (only at the end of the sequence, where B = 0) get no
+// decay and rho = 1, which leaves the state unchanged.
 template <typename T, int NM, bool SP, bool WY, bool ST, bool FULL>
 MM_DEV void compute_half(const uint4& tu, const uint4& td, const uint4& tz, const float* __restrict__ sB,
                          const float* __restrict__ sC, int kb, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
-                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, bool has_z,
+                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, float& s_prev, bool has_z,
                          float (&yk)[Stage<T, NM>::HT]) {
   constexpr int HT = Stage<T, NM>::HT;
+  constexpr int HP = HT / 2;
   constexpr int PS = Stage<T, NM>::PS;
-  float dk[HT];   // ST: exp(delta*A[0]); general: delta * log2(e)
-  float duk[HT];  // delta * u
-  float gk[HT];   // WY: SiLU(z) (1 without z)
+  // Per-step scalars, held as pairs of consecutive steps (2kp, 2kp + 1).
+  f2_t rk2[HP];   // ST: exp(delta*A[0]); general: delta * log2(e)
+  f2_t rho2[HP];  // s_{k-1} / s_k
+  f2_t sk2[HP];   // WY: s_k
+  f2_t gk2[HP];   // WY: SiLU(z) (1 without z)
+  f2_t yd2[HP];   // WY: D * u
+  float sp = s_prev;
+  f2_t dsum = f2_pack(0.f, 0.f);
 #pragma unroll
-  for (int kp = 0; kp < HT / 2; ++kp) {
-    const float2 xs = vec_pair<T>(tu, kp);
-    const float2 drs = vec_pair<T>(td, kp);
-    float2 zs = make_float2(0.f, 0.f);
-    if (WY && has_z) zs = vec_pair<T>(tz, kp);
-#pragma unroll
-    for (int s2 = 0; s2 < 2; ++s2) {
-      const int k = 2 * kp + s2;
-      const float x = s2 ? xs.y : xs.x;
-      const float dr = s2 ? drs.y : drs.x;
-      float d2 = SP ? softplus_log2(dr) : dr * kLog2e;
-      if (!FULL && k >= nsteps) d2 = 0.f;  // steps past the end: no decay, no input
-      sum_d2 += d2;
-      if (!SP) min_d2 = fminf(min_d2, d2);
-      dk[k] = ST ? ex2(d2 * A0) : d2;
-      duk[k] = d2 * x;
-      if (WY) {
-        yk[k] = Dv * x;
-        gk[k] = has_z ? silu(s2 ? zs.y : zs.x) : 1.0f;
-      }
+  for (int kp = 0; kp < HP; ++kp) {
+    const float2 xf = vec_pair<T>(tu, kp);
+    const float2 df = vec_pair<T>(td, kp);
+    const f2_t x2 = f2_pack(xf.x, xf.y);
+    f2_t d2 = SP ? softplus_log2_2(f2_pack(df.x, df.y)) : f2_mul(f2_pack(df.x, df.y), f2_pack(kLog2e, kLog2e));
+    const bool live0 = FULL || 2 * kp < nsteps;
+    const bool live1 = FULL || 2 * kp + 1 < nsteps;
+    if (!FULL) {
+      const float2 dd = f2_unpack(d2);
+      d2 = f2_pack(live0 ? dd.x : 0.f, live1 ? dd.y : 0.f);
+    }
+    dsum = f2_add(dsum, d2);
+    if (!SP) {
+      const float2 dd = f2_unpack(d2);
+      min_d2 = fminf(min_d2, fminf(dd.x, dd.y));
+    }
+    float2 ss = f2_unpack(f2_mul(d2, x2));
+    ss.x = fabsf(ss.x) >= kMinScale ? ss.x : copysignf(kMinScale, ss.x);
+    ss.y = fabsf(ss.y) >= kMinScale ? ss.y : copysignf(kMinScale, ss.y);
+    if (!FULL) {
+      ss.x = live0 ? ss.x : sp;
+      ss.y = live1 ? ss.y : ss.x;
+    }
+    const f2_t s2 = f2_pack(ss.x, ss.y);
+    f2_t inv2;
+    if (WY && has_z) {
+      const float2 zf = vec_pair<T>(tz, kp);
+      const f2_t z2 = f2_pack(zf.x, zf.y);
+      const float2 ez = f2_unpack(f2_mul(z2, f2_pack(-kLog2e, -kLog2e)));
+      const f2_t ope = f2_add(f2_pack(fminf(ex2(ez.x), kMaxExpZ), fminf(ex2(ez.y), kMaxExpZ)), f2_pack(1.f, 1.f));
+      const float2 den = f2_unpack(f2_mul(s2, ope));
+      const f2_t q = f2_pack(rcp(den.x), rcp(den.y));
+      inv2 = f2_mul(ope, q);
+      gk2[kp] = f2_mul(z2, f2_mul(s2, q));
+    } else {
+      inv2 = f2_pack(rcp(ss.x), rcp(ss.y));
+      if (WY) gk2[kp] = f2_pack(1.f, 1.f);
+    }
+    rho2[kp] = f2_mul(f2_pack(sp, ss.x), inv2);
+    if (!FULL) {
+      const float2 rr = f2_unpack(rho2[kp]);
+      rho2[kp] = f2_pack(live0 ? rr.x : 1.f, live1 ? rr.y : 1.f);
+    }
+    sp = ss.y;
+    if (WY) {
+      sk2[kp] = s2;
+      yd2[kp] = f2_mul(x2, f2_pack(Dv, Dv));
+    }
+    if (ST) {
+      const float2 a = f2_unpack(f2_mul(d2, f2_pack(A0, A0)));
+      rk2[kp] = f2_pack(ex2(a.x), ex2(a.y));
+    } else {
+      rk2[kp] = d2;
     }
   }
+  {
+    const float2 ds = f2_unpack(dsum);
+    sum_d2 += ds.x + ds.y;
+  }
+  s_prev = sp;
   constexpr int SK = HT < MM_SCAN_SUBTILE ? HT : MM_SCAN_SUBTILE;  // steps per pass over the state pairs
+  // General A: the exponentials of the last kPolyPairs state pairs run as polynomials on the FMA pipe, the
+  // rest on the MUFU, so that both pipes carry a similar load.
+  constexpr int kPolyPairs = (NM / 2) * MM_SCAN_POLY_EIGHTHS / 8;
 #pragma unroll
   for (int k0 = 0; k0 < HT; k0 += SK) {
-    f2_t a[SK], rr[SK], du2[SK], dd2[SK], y2[SK];
+    f2_t c[SK], rr[SK], acc[SK];
 #pragma unroll
     for (int j = 0; j < SK; ++j) {
       const int k = k0 + j;
-      du2[j] = f2_pack(duk[k], duk[k]);
-      y2[j] = f2_pack(0.f, 0.f);
+      const float2 rp = f2_unpack(rk2[k >> 1]);
+      const float2 hp = f2_unpack(rho2[k >> 1]);
+      const float r = (k & 1) ? rp.y : rp.x;
+      const float rho = (k & 1) ? hp.y : hp.x;
+      acc[j] = f2_pack(0.f, 0.f);
       if (ST) {
-        const float r = dk[k];
         const float r2 = r * r;
-        a[j] = f2_pack(r, r2);
+        c[j] = f2_pack(rho * r, rho * r2);
         rr[j] = f2_pack(r2, r2);
       } else {
-        dd2[j] = f2_pack(dk[k], dk[k]);
+        c[j] = f2_pack(r, r);       // delta2, both lanes
+        rr[j] = f2_pack(rho, rho);  // rho, both lanes
       }
     }
 #pragma unroll
@@ -292,41 +359,49 @@ MM_DEV void compute_half(const uint4& tu, const uint4& td, const uint4& tz, cons
       }
 #pragma unroll
       for (int j = 0; j < SK; ++j) {
-        if (FULL || k0 + j < nsteps) {
-          const float4& b4 = bq[j >> 1];
-          const f2_t bb = (j & 1) ? f2_pack(b4.z, b4.w) : f2_pack(b4.x, b4.y);
-          f2_t ap;
-          if (ST) {
-            if (pi > 0) a[j] = f2_mul(a[j], rr[j]);
-            ap = a[j];
+        const float4& b4 = bq[j >> 1];
+        const f2_t bb = (j & 1) ? f2_pack(b4.z, b4.w) : f2_pack(b4.x, b4.y);
+        f2_t cp;
+        if (ST) {
+          if (pi > 0) c[j] = f2_mul(c[j], rr[j]);
+          cp = c[j];
+        } else {
+          const f2_t arg = f2_mul(c[j], A2[pi]);
+          f2_t e;
+          if (pi >= NM / 2 - kPolyPairs) {
+            e = exp2_poly2(arg);  // FMA pipe
           } else {
-            const float2 arg = f2_unpack(f2_mul(dd2[j], A2[pi]));
-            ap = f2_pack(ex2(arg.x), ex2(arg.y));
+            const float2 a = f2_unpack(arg);
+            e = f2_pack(ex2(a.x), ex2(a.y));  // MUFU
           }
-          h[pi] = f2_fma(ap, h[pi], f2_mul(du2[j], bb));
-          if (WY) {
-            const float4& c4 = cq[j >> 1];
-            y2[j] = f2_fma(h[pi], (j & 1) ? f2_pack(c4.z, c4.w) : f2_pack(c4.x, c4.y), y2[j]);
-          }
+          cp = f2_mul(rr[j], e);
+        }
+        h[pi] = f2_fma(cp, h[pi], bb);
+        if (WY) {
+          const float4& c4 = cq[j >> 1];
+          acc[j] = f2_fma(h[pi], (j & 1) ? f2_pack(c4.z, c4.w) : f2_pack(c4.x, c4.y), acc[j]);
         }
       }
     }
     if (WY) {
 #pragma unroll
-      for (int j = 0; j < SK; ++j) {
-        const float2 ys = f2_unpack(y2[j]);
-        yk[k0 + j] = (yk[k0 + j] + (ys.x + ys.y)) * gk[k0 + j];
+      for (int j = 0; j < SK; j += 2) {
+        const int kp = (k0 + j) >> 1;
+        const float2 a0 = f2_unpack(acc[j]);
+        const float2 a1 = f2_unpack(acc[j + 1]);
+        const float2 y = f2_unpack(f2_mul(f2_fma(sk2[kp], f2_pack(a0.x + a0.y, a1.x + a1.y), yd2[kp]), gk2[kp]));
+        yk[k0 + j] = y.x;
+        yk[k0 + j + 1] = y.y;
       }
     }
   }
 }
 
-// One staged tile = two half tiles. A full tile (the common case) is one branch-free block, so the
-// scheduler can overlap the second half's MUFU-heavy phase 1 with the first half's FMA-heavy phase 2.
+// One staged tile = two half tiles. A full tile (the common case) is one branch-free block.
 template <typename T, int NM, bool SP, bool WY, bool ST, bool FULLTILE>
 MM_DEV void compute_tile_t(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
-                           float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
-                           const Params& p, int t0, int lane) {
+                           float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, float& s_prev,
+                           const Lane<T>& ln, const Params& p, int t0, int lane) {
   constexpr int HT = Stage<T, NM>::HT;
   const float* sB = sm.bc;
   const float* sC = sm.bc + Stage<T, NM>::COFF;
@@ -340,11 +415,11 @@ MM_DEV void compute_tile_t(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2
     uint4 tz = make_uint4(0, 0, 0, 0);
     if (WY && p.has_z) tz = sm.io[slot][2][lane][v];
     if (FULLTILE || ns >= HT)
-      compute_half<T, NM, SP, WY, ST, true>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, HT, sum_d2, min_d2, p.has_z,
-                                           yk[v]);
+      compute_half<T, NM, SP, WY, ST, true>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, HT, sum_d2, min_d2, s_prev,
+                                           p.has_z, yk[v]);
     else
-      compute_half<T, NM, SP, WY, ST, false>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, ns, sum_d2, min_d2, p.has_z,
-                                            yk[v]);
+      compute_half<T, NM, SP, WY, ST, false>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, ns, sum_d2, min_d2, s_prev,
+                                            p.has_z, yk[v]);
   }
   if (WY && ln.active) {
 #pragma unroll
@@ -368,12 +443,14 @@ MM_DEV void compute_tile_t(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2
 
 template <typename T, int NM, bool SP, bool WY, bool ST>
 MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
-                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, const Lane<T>& ln,
-                         const Params& p, int t0, int lane) {
+                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, float& s_prev,
+                         const Lane<T>& ln, const Params& p, int t0, int lane) {
   if (nsteps == Stage<T, NM>::TT)
-    compute_tile_t<T, NM, SP, WY, ST, true>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
+    compute_tile_t<T, NM, SP, WY, ST, true>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, s_prev, ln, p, t0,
+                                            lane);
   else
-    compute_tile_t<T, NM, SP, WY, ST, false>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, ln, p, t0, lane);
+    compute_tile_t<T, NM, SP, WY, ST, false>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, s_prev, ln, p, t0,
+                                             lane);
 }
 
 // Runs the recurrence over timesteps [t_begin, t_end) (t_begin tile-aligned), keeping kStages - 1
@@ -396,6 +473,7 @@ MM_DEV int run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end,
     if (!p.use_tma) cp_async_commit();
   }
   int t_done = t_end;
+  float s_prev = 1.0f;  // h holds the scaled state g = h / s_prev inside the loop; g = h at the start
   for (int i = 0; i < ntiles; ++i) {
     const int nx = i + kStages - 1;
     if (nx < ntiles) issue_tile<T, NM>(sm, nx % kStages, p, ln, t_begin + nx * TT, lane);
@@ -410,7 +488,8 @@ MM_DEV int run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end,
     convert_bc<T, NM>(sm, slot, lane);
     __syncwarp();
     const int t0 = t_begin + i * TT;
-    compute_tile<T, NM, SP, WY, ST>(sm, slot, h, A2, A0, Dv, min(TT, t_end - t0), sum_d2, min_d2, ln, p, t0, lane);
+    compute_tile<T, NM, SP, WY, ST>(sm, slot, h, A2, A0, Dv, min(TT, t_end - t0), sum_d2, min_d2, s_prev, ln, p, t0,
+                                    lane);
     __syncwarp();  // B/C buffer and this slot are free for the next iteration
     if (t0 + TT >= stop_from && t0 + TT < t_end &&
         __all_sync(0xffffffffu, decays && (A_max * sum_d2 <= kDecayCutoffLog2))) {
@@ -424,6 +503,9 @@ MM_DEV int run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end,
   }
   if (!p.use_tma) cp_async_wait<0>();
   __syncwarp();
+  const f2_t sc = f2_pack(s_prev, s_prev);
+#pragma unroll
+  for (int q = 0; q < NM / 2; ++q) h[q] = f2_mul(h[q], sc);  // back to the true state
   return t_done;
 }
 

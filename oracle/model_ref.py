@@ -47,8 +47,23 @@ def scan_seq(u, delta, A, B, C, D, z, delta_softplus=True):
     return y, h
 
 
+def _identity(x):
+    return x
+
+
+def rounder(act_dtype):
+    """Rounding of an activation to the dtype the reference stores it in. With bf16 / fp16 weights MLX
+    keeps every layer output in the weights' dtype (matmul, conv and elementwise ops return their input
+    dtype, accumulating internally in float32); the oracle then computes in float32 and rounds each such
+    output to ``act_dtype``. None (or float32) = no rounding."""
+    if act_dtype is None or act_dtype == torch.float32:
+        return _identity
+    return lambda x: x.to(act_dtype).to(torch.float32)
+
+
 class RefMixer:
-    def __init__(self, sd: dict, prefix: str, d_state: int, dt_rank: int, dtype=torch.float32):
+    def __init__(self, sd: dict, prefix: str, d_state: int, dt_rank: int, dtype=torch.float32, act_dtype=None):
+        self.q = rounder(act_dtype)
         g = lambda k: sd[prefix + k].to(dtype)
         self.W_in, self.W_x, self.W_dt, self.b_dt = g("in_proj.weight"), g("x_proj.weight"), g("dt_proj.weight"), \
             g("dt_proj.bias")
@@ -68,16 +83,16 @@ class RefMixer:
         return out + self.conv_b
 
     def _core(self, x):
-        E, N, R = self.E, self.N, self.R
-        xz = x @ self.W_in.T
+        E, N, R, q = self.E, self.N, self.R, self.q
+        xz = q(x @ self.W_in.T)
         xm, z = xz[..., :E], xz[..., E:]
-        xc = _silu(self._conv(xm))
-        x_dbl = xc @ self.W_x.T
-        dt = x_dbl[..., :R] @ self.W_dt.T + self.b_dt
+        xc = q(_silu(self._conv(xm)))
+        x_dbl = q(xc @ self.W_x.T)
+        dt = q(x_dbl[..., :R] @ self.W_dt.T + self.b_dt)
         Bm, Cm = x_dbl[..., R:R + N], x_dbl[..., R + N:]
         y, h = scan_seq(xc.transpose(1, 2), dt.transpose(1, 2), self.A, Bm.transpose(1, 2), Cm.transpose(1, 2),
                         self.D, z.transpose(1, 2), delta_softplus=True)
-        return y.transpose(1, 2) @ self.W_out.T, xm, h
+        return q(q(y.transpose(1, 2)) @ self.W_out.T), xm, h
 
     def forward(self, x):
         return self._core(x)[0]
@@ -91,66 +106,82 @@ class RefMixer:
 
     def step(self, x_tok, conv_state, ssm_state):
         """mamba_block.py:155-198 (softplus without cutoff, as nn.softplus)."""
-        E, N, R = self.E, self.N, self.R
-        xz = x_tok[:, 0] @ self.W_in.T
+        E, N, R, q = self.E, self.N, self.R, self.q
+        xz = q(x_tok[:, 0] @ self.W_in.T)
         xm, z = xz[:, :E], xz[:, E:]
         new_conv = torch.cat([conv_state[:, :, 1:], xm[:, :, None]], dim=2)
-        xc = _silu((new_conv * self.conv_w[None]).sum(-1) + self.conv_b)
-        x_dbl = xc @ self.W_x.T
-        dt = F.softplus(x_dbl[:, :R] @ self.W_dt.T + self.b_dt)
+        xc = q(_silu((new_conv * self.conv_w[None]).sum(-1) + self.conv_b))
+        x_dbl = q(xc @ self.W_x.T)
+        dt = F.softplus(q(x_dbl[:, :R] @ self.W_dt.T + self.b_dt))
         Bm, Cm = x_dbl[:, R:R + N], x_dbl[:, R + N:]
         new_ssm = torch.exp(dt[:, :, None] * self.A[None]) * ssm_state + (dt * xc)[:, :, None] * Bm[:, None, :]
         y = (new_ssm * Cm[:, None, :]).sum(-1) + self.D * xc
-        y = y * _silu(z)
-        return (y @ self.W_out.T)[:, None, :], new_conv, new_ssm
+        y = q(y * _silu(z))
+        return q(y @ self.W_out.T)[:, None, :], new_conv, new_ssm
 
 
 class RefModel:
     """Reference model over a MambaModel state_dict (float32)."""
 
-    def __init__(self, sd: dict, cfg, dtype=torch.float32, device="cpu"):
+    def __init__(self, sd: dict, cfg, dtype=torch.float32, device="cpu", act_dtype=None):
+        """``act_dtype`` (e.g. torch.bfloat16): round every projection, conv, scan and RMSNorm output to it,
+        as the reference does for a model whose weights are in that dtype (see ``rounder``); the residual
+        stream stays float32."""
         sd = {k: v.to(device) for k, v in sd.items()}
         dt_rank = cfg.dt_rank if cfg.dt_rank is not None else -(-cfg.d_model // 16)
         self.cfg = cfg
+        self.q = rounder(act_dtype)
         self.emb = sd["embeddings.weight"].to(dtype)
         self.norms = [sd[f"layers.{i}.norm.weight"].to(dtype) for i in range(cfg.n_layer)]
-        self.mixers = [RefMixer(sd, f"layers.{i}.mixer.", cfg.d_state, dt_rank, dtype) for i in range(cfg.n_layer)]
+        self.mixers = [RefMixer(sd, f"layers.{i}.mixer.", cfg.d_state, dt_rank, dtype, act_dtype)
+                       for i in range(cfg.n_layer)]
         self.norm_f = sd["norm_f.weight"].to(dtype)
         self.eps = cfg.rms_norm_eps
+
+    def set_act_dtype(self, act_dtype):
+        """Switches the activation rounding (see ``rounder``) of the model and of every mixer."""
+        self.q = rounder(act_dtype)
+        for m in self.mixers:
+            m.q = self.q
+
+    def _head(self, x):
+        """Final RMSNorm and tied head (mamba_model.py:76-78)."""
+        return self.q(self.q(rmsnorm(x, self.norm_f, self.eps)) @ self.emb.T)
 
     def forward(self, ids):
         x = self.emb[ids]
         for w, m in zip(self.norms, self.mixers):
-            x = x + m.forward(rmsnorm(x, w, self.eps))
-        return rmsnorm(x, self.norm_f, self.eps) @ self.emb.T
+            x = x + m.forward(self.q(rmsnorm(x, w, self.eps)))
+        return self._head(x)
 
     def prefill(self, ids, last_only=False):
         x = self.emb[ids]
         convs, ssms = [], []
         for w, m in zip(self.norms, self.mixers):
-            y, cs, ss = m.prefill(rmsnorm(x, w, self.eps))
+            y, cs, ss = m.prefill(self.q(rmsnorm(x, w, self.eps)))
             x = x + y
             convs.append(cs)
             ssms.append(ss)
         if last_only:
             x = x[:, -1:]
-        return rmsnorm(x, self.norm_f, self.eps) @ self.emb.T, convs, ssms
+        return self._head(x), convs, ssms
 
     def step(self, ids, convs, ssms):
         x = self.emb[ids]
         nc, ns = [], []
         for w, m, cs, ss in zip(self.norms, self.mixers, convs, ssms):
-            y, c2, s2 = m.step(rmsnorm(x, w, self.eps), cs, ss)
+            y, c2, s2 = m.step(self.q(rmsnorm(x, w, self.eps)), cs, ss)
             x = x + y
             nc.append(c2)
             ns.append(s2)
-        return rmsnorm(x, self.norm_f, self.eps) @ self.emb.T, nc, ns
+        return self._head(x), nc, ns
 
-    def greedy(self, ids, n_new, forced=None):
+    def greedy(self, ids, n_new, forced=None, prefilled=None):
         """Greedy prefill -> step loop (generate.py:82-108). If ``forced`` (B, n_new) is given the loop is
         teacher-forced with those tokens, so one near-tie does not cascade; returns (tokens, per-step
-        logits) with tokens the argmax at each step."""
-        logits, convs, ssms = self.prefill(ids, last_only=True)
+        logits) with tokens the argmax at each step. ``prefilled`` = the (logits, convs, ssms) of an
+        earlier ``prefill(ids, last_only=True)`` skips the prefill (steps never modify those states)."""
+        logits, convs, ssms = prefilled if prefilled is not None else self.prefill(ids, last_only=True)
         nxt = logits[:, -1]
         toks, all_logits = [], []
         for i in range(n_new):
@@ -161,3 +192,13 @@ class RefModel:
             lg, convs, ssms = self.step(feed[:, None], convs, ssms)
             nxt = lg[:, 0]
         return torch.stack(toks, 1), torch.stack(all_logits, 1)
+
+
+def sampling_probs(next_logits, temperature):
+    """Distribution of the sampled next id at temperature T > 0: mx.random.categorical(logits / T)
+    (generate.py:42-44, :92-93) draws index k with probability softmax(logits / T)_k. float64."""
+    x = next_logits.double() / temperature
+    x = x - x.max(dim=-1, keepdim=True).values
+    e = torch.exp(x)
+    return e / e.sum(dim=-1, keepdim=True)
+
