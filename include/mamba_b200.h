@@ -285,6 +285,34 @@ int mm_peer_allreduce_add_rmsnorm(const MMPeerAddNormArgs* args, mm_stream_t str
 int mm_exp2_check(const float* x, float* y_poly, float* y_mufu, int64_t n, mm_stream_t stream);
 
 /* Library version string (static storage). */
+/* ---------------------------------------------------------------------------------------------
+ * Dense projection of the decode step: y = x @ w^T (+ bias), bf16 inputs, fp32 accumulation.
+ *   x: (M, K) bf16, row stride ldx;  w: (N, K) bf16, row stride ldw (the nn.Linear weight layout);
+ *   bias: (N,) fp32 or NULL;  y: (M, N) of y_dtype (MM_F32 or MM_BF16), row stride ldy.
+ * Replaces the nn.Linear calls of the decode step, mamba_metal/mamba_block.py:167 (in_proj), :179
+ * (x_proj), :181 (dt_proj) and :197 (out_proj); the same shapes serve any small-M product. Base
+ * pointers and row strides of x and w must be 16-byte aligned (TMA). splits = 0 lets the library split
+ * K over CTAs so that every SM streams weights; split partials are summed in a fixed order by the last
+ * CTA of each output tile, so the result does not depend on scheduling. The workspace (size from
+ * mm_linear_workspace_size, 256-byte aligned) must be zero-filled before its first use; every call
+ * leaves it zeroed again. Calls sharing a workspace must not overlap on the GPU.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct MMLinearArgs {
+  const void* x;
+  const void* w;
+  const float* bias; /* may be NULL */
+  void* y;
+  int64_t ldx, ldw, ldy;
+  int64_t y_dtype;
+  int64_t M, N, K;
+  int64_t splits; /* 0 = chosen by the library */
+} MMLinearArgs;
+
+int mm_linear_workspace_size(const MMLinearArgs* args, size_t* bytes);
+int mm_linear_fwd(const MMLinearArgs* args, void* workspace, size_t workspace_bytes, mm_stream_t stream);
+/* Synchronises `stream`; MM_ERR_TIMEOUT if a pipeline wait of a call on `workspace` ran out. */
+int mm_linear_status(const void* workspace, mm_stream_t stream);
+
 const char* mm_version(void);
 
 #ifdef __cplusplus

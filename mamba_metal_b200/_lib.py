@@ -92,6 +92,13 @@ class MMPeerAddNormArgs(ctypes.Structure):
     ]
 
 
+class MMLinearArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _p), ("w", _p), ("bias", _p), ("y", _p), ("ldx", _i64), ("ldw", _i64), ("ldy", _i64),
+        ("y_dtype", _i64), ("M", _i64), ("N", _i64), ("K", _i64), ("splits", _i64),
+    ]
+
+
 _SIGNATURES = {
     "mm_selective_scan_workspace_size": ([ctypes.POINTER(MMScanArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "mm_selective_scan_fwd": ([ctypes.POINTER(MMScanArgs), _p, ctypes.c_size_t, _p], ctypes.c_int),
@@ -105,6 +112,9 @@ _SIGNATURES = {
     "mm_peer_allreduce": ([ctypes.POINTER(MMPeerReduceArgs), _p], ctypes.c_int),
     "mm_peer_allreduce_add_rmsnorm": ([ctypes.POINTER(MMPeerAddNormArgs), _p], ctypes.c_int),
     "mm_exp2_check": ([_p, _p, _p, _i64, _p], ctypes.c_int),
+    "mm_linear_workspace_size": ([ctypes.POINTER(MMLinearArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "mm_linear_fwd": ([ctypes.POINTER(MMLinearArgs), _p, ctypes.c_size_t, _p], ctypes.c_int),
+    "mm_linear_status": ([_p, _p], ctypes.c_int),
     "mm_version": ([], ctypes.c_char_p),
 }
 

@@ -11,7 +11,9 @@ dt_proj, A_log, D, out_proj). Differences, all deliberate:
   to MLX's (d_inner, d_conv, 1) at load_hf.py:46-50).
 - ``step`` returns new state tensors like the reference by default; ``step(..., inplace=True)``
   updates the given conv / SSM state tensors in place (O(1) memory), which generation uses.
-- The dense projections are cuBLAS GEMMs through torch; everything else runs in libmamba_b200.so.
+- The dense projections are cuBLAS GEMMs through torch; those of the decode step (``step``) can run on
+  the library's tcgen05 small-batch GEMM (``ops.linear``) instead (``USE_DECODE_GEMM``); everything
+  else runs in libmamba_b200.so.
 """
 
 from __future__ import annotations
@@ -24,6 +26,29 @@ from torch import nn
 
 from mamba_metal_b200 import ops
 from mamba_metal_b200.selective_scan import selective_scan_into
+
+# With USE_DECODE_GEMM, decode-step projections of bf16 weights with at most DECODE_GEMM_MAX_ROWS token
+# rows use ops.linear (tcgen05, weight-streaming, split-K) instead of cuBLAS. Off by default: measured on
+# B200 at configs[3] (batch 64) the cuBLAS projections are faster (53.5 vs 73.1 us per layer).
+USE_DECODE_GEMM = False
+DECODE_GEMM_MAX_ROWS = 256
+
+
+def decode_linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None, bias32: torch.Tensor | None = None) -> torch.Tensor:
+    """x @ w.T (+ bias) for a decode step's (rows, K) activation: the library's small-batch GEMM when it
+    applies (bf16, 16-byte aligned rows), cuBLAS otherwise. ``bias32`` is the bias in float32 for the
+    library path (converted from ``bias`` when not given)."""
+    if (USE_DECODE_GEMM and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2
+            and x.shape[0] <= DECODE_GEMM_MAX_ROWS and x.stride(1) == 1 and w.stride(1) == 1
+            and x.stride(0) % 8 == 0 and w.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0):
+        return ops.linear(x, w, bias32 if bias32 is not None else bias, out=out)
+    if out is None:
+        return F.linear(x, w, bias)
+    torch.matmul(x, w.t(), out=out)
+    if bias is not None:
+        out += bias
+    return out
 
 
 class MambaBlock(nn.Module):
@@ -58,7 +83,7 @@ class MambaBlock(nn.Module):
         """x @ w.T; for a tensor-parallel block (x_proj, out_proj are row-parallel) the partial products
         are all-reduced over the group (site 0: x_proj, 1: out_proj)."""
         if self.tp_reduce is None:
-            return F.linear(x, w)
+            return decode_linear(x, w) if x.dim() == 2 else F.linear(x, w)
         return self.tp_reduce(x, w, self.tp_sites[site])
 
     # A = -exp(A_log) (mamba_block.py:87, :138), cached until A_log changes
@@ -67,6 +92,14 @@ class MambaBlock(nn.Module):
         if self._A_cache is None or self._A_cache[0] != key:
             self._A_cache = (key, (-torch.exp(self.A_log.float())).contiguous())
         return self._A_cache[1]
+
+    # dt_proj's bias in float32 for the decode GEMM's epilogue, cached until the parameter changes
+    def _dt_bias32(self) -> torch.Tensor:
+        b = self.dt_proj.bias
+        key = (b.data_ptr(), b._version, b.device)
+        if getattr(self, "_dt_bias_cache", None) is None or self._dt_bias_cache[0] != key:
+            self._dt_bias_cache = (key, b.detach().float().contiguous())
+        return self._dt_bias_cache[1]
 
     def _run(self, x: torch.Tensor, want_state: bool):
         bsz, L, _ = x.shape
@@ -112,11 +145,11 @@ class MambaBlock(nn.Module):
             conv_state = conv_state.to(torch.float32, copy=True).contiguous()
         if not inplace or ssm_state.dtype != torch.float32 or not ssm_state.is_contiguous():
             ssm_state = ssm_state.to(torch.float32, copy=True).contiguous()
-        xz = F.linear(x_token[:, 0].to(dt_), self.in_proj.weight)       # (B, 2E)
+        xz = decode_linear(x_token[:, 0].to(dt_), self.in_proj.weight)  # (B, 2E)
         xc = ops.causal_conv1d_step(xz[:, :E], conv_state, self.conv1d.weight, self.conv1d.bias, silu=True)
         x_dbl = self._project(xc, self.x_proj.weight, 0)                    # (B, R + 2N)
         Df = self.D if self.D.dtype == torch.float32 else self.D.float()
-        dt = F.linear(x_dbl[:, :R], self.dt_proj.weight, self.dt_proj.bias)
+        dt = decode_linear(x_dbl[:, :R], self.dt_proj.weight, self.dt_proj.bias, bias32=self._dt_bias32())
         y = ops.ssm_decode_step(xc, dt, xz[:, E:], x_dbl[:, R:R + N], x_dbl[:, R + N:], self._A(), Df,
                                 ssm_state, dt_softplus=True)
         if defer_out and self.tp_reduce is not None and hasattr(self.tp_reduce, "partial"):

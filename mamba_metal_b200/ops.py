@@ -136,3 +136,61 @@ def add_rmsnorm(residual: torch.Tensor, delta: torch.Tensor | None, weight: torc
         rc = _lib.lib().mm_add_rmsnorm(ctypes.byref(a), _lib.stream_handle(dev))
     _lib.check(rc, "mm_add_rmsnorm")
     return out
+
+
+_LINEAR_WS: dict[int, torch.Tensor] = {}
+
+
+def _linear_workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-filled workspace of mm_linear_fwd for this device (every call leaves it zeroed again); grown
+    when a larger call needs it. Grow it before capturing a CUDA graph (an eager call of the same shapes
+    does that)."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _LINEAR_WS.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _LINEAR_WS[idx] = ws
+    return ws
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, *, out_dtype: torch.dtype | None = None,
+           out: torch.Tensor | None = None, splits: int = 0) -> torch.Tensor:
+    """y = x @ w.T (+ bias) for bf16 x (M, K) and w (N, K) (nn.Linear layout), fp32 accumulation, on the
+    tcgen05 decode GEMM of libmamba_b200.so (mm_linear_fwd). The decode step's projections
+    (mamba_metal/mamba_block.py:167, :179, :181, :197) go through here. out_dtype: bfloat16 (default) or
+    float32; ``out`` may be a (M, N) view with unit inner stride."""
+    M, K = x.shape
+    N = w.shape[0]
+    assert w.shape[1] == K and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+    assert x.stride(1) == 1 and w.stride(1) == 1
+    dev = _lib.require_cuda(x, w, bias, out)
+    odt = out_dtype or (out.dtype if out is not None else torch.bfloat16)
+    if out is None:
+        out = torch.empty((M, N), dtype=odt, device=dev)
+    assert out.shape == (M, N) and out.dtype == odt and out.stride(1) == 1
+    b = None if bias is None else (bias if bias.dtype == torch.float32 and bias.is_contiguous() else
+                                   bias.float().contiguous())
+    a = _lib.MMLinearArgs()
+    a.x, a.w, a.bias, a.y = x.data_ptr(), w.data_ptr(), _lib.ptr(b), out.data_ptr()
+    a.ldx, a.ldw, a.ldy = x.stride(0), w.stride(0), out.stride(0)
+    a.y_dtype = _lib.DTYPE_CODE[odt]
+    a.M, a.N, a.K, a.splits = M, N, K, int(splits)
+    lib = _lib.lib()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(lib.mm_linear_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)), "mm_linear_workspace_size")
+    ws = _linear_workspace(dev, int(nbytes.value))
+    with torch.cuda.device(dev):
+        rc = lib.mm_linear_fwd(ctypes.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_handle(dev))
+    _lib.check(rc, "mm_linear_fwd")
+    return out
+
+
+def linear_status(device: torch.device | int | None = None) -> int:
+    """Status word of the device's linear workspace: 0, or MM_ERR_TIMEOUT after a pipeline wait ran out."""
+    dev = torch.device("cuda", device) if isinstance(device, int) else (device or torch.device("cuda"))
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _LINEAR_WS.get(idx)
+    if ws is None:
+        return 0
+    with torch.cuda.device(dev):
+        return _lib.lib().mm_linear_status(ws.data_ptr(), _lib.stream_handle(dev))

@@ -20,6 +20,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
+from mamba_metal_b200.mamba_block import decode_linear
 from mamba_metal_b200.mamba_model import MambaConfig, MambaModel
 
 
@@ -68,7 +69,7 @@ class _TPProject:
         peer = self.peer
         if peer is not None and rows <= self.max_rows and x.dtype == peer.dtype and n <= peer.capacity[site]:
             part = peer.slot(site)[:n].view(rows, w.shape[0])
-            torch.matmul(x.reshape(rows, x.shape[-1]), w.t(), out=part)
+            decode_linear(x.reshape(rows, x.shape[-1]), w, out=part)
             out = torch.empty((rows, w.shape[0]), dtype=x.dtype, device=x.device)
             peer.reduce(site, n, out)
             return out.view(*x.shape[:-1], w.shape[0])
@@ -87,7 +88,7 @@ class _TPProject:
                 or n * peer.esize > peer.ll_max_bytes:
             return None
         part = peer.slot(site)[:n].view(rows, w.shape[0])
-        torch.matmul(x.reshape(rows, x.shape[-1]), w.t(), out=part)
+        decode_linear(x.reshape(rows, x.shape[-1]), w, out=part)
         return _PendingReduce(peer, site, rows, w.shape[0])
 
 
