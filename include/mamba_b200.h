@@ -61,7 +61,8 @@ enum {
 
 /* ---------------------------------------------------------------------------------------------
  * Selective scan forward.
- *   delta' = softplus(delta) if delta_softplus else delta        (softplus uses the >20 cutoff)
+ *   delta' = softplus(delta + delta_bias[d]) if delta_softplus else delta + delta_bias[d]
+ *            (softplus uses the >20 cutoff; delta_bias is optional, 0 when NULL)
  *   h[t,n] = exp(delta'[t] * A[d,n]) * h[t-1,n] + delta'[t] * u[t] * B[n,t],   h[-1] = 0
  *   y[t]   = (sum_n h[t,n] * C[n,t] + D[d] * u[t]) * silu(z[t])   (D and z optional)
  *   state_out[b,d,n] = h[seqlen-1, n]
@@ -100,6 +101,9 @@ typedef struct MMScanArgs {
   int64_t delta_softplus; /* 0 / 1 */
   int64_t piece_tiles;    /* timestep tiles per warp; 0 = chosen by the library */
   int64_t options;        /* bit 0: stage tiles with cp.async / plain loads instead of TMA */
+  const float* delta_bias; /* (dim,) fp32 added to delta before softplus, or NULL. No counterpart in the
+                              reference's kernel: the dt_proj bias of a Mamba block (mamba_block.py:85),
+                              applied here so that dt_proj's GEMM needs no separate bias pass */
 } MMScanArgs;
 
 int mm_selective_scan_workspace_size(const MMScanArgs* args, size_t* bytes);

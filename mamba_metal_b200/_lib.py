@@ -36,7 +36,7 @@ class MMScanArgs(ctypes.Structure):
         ("state_out", _p), ("dtype", _i64), ("batch", _i64), ("dim", _i64), ("dstate", _i64), ("seqlen", _i64),
         ("u_stride", _i64 * 3), ("delta_stride", _i64 * 3), ("z_stride", _i64 * 3), ("y_stride", _i64 * 3),
         ("B_stride", _i64 * 3), ("C_stride", _i64 * 3), ("A_stride", _i64 * 2),
-        ("delta_softplus", _i64), ("piece_tiles", _i64), ("options", _i64),
+        ("delta_softplus", _i64), ("piece_tiles", _i64), ("options", _i64), ("delta_bias", _p),
     ]
 
 

@@ -164,7 +164,7 @@ extern "C" int mm_selective_scan_fwd(const MMScanArgs* a, void* ws, size_t ws_by
   const int es = dtype_size(a->dtype);
   Params p;
   p.u = a->u; p.delta = a->delta; p.z = a->z; p.y = a->y; p.Bm = a->B; p.Cm = a->C;
-  p.A = a->A; p.D = a->D; p.state_out = a->state_out;
+  p.A = a->A; p.D = a->D; p.dbias = a->delta_bias; p.state_out = a->state_out;
   for (int i = 0; i < 3; ++i) {
     p.us[i] = a->u_stride[i]; p.ds[i] = a->delta_stride[i]; p.zs[i] = a->z_stride[i];
     p.ys[i] = a->y_stride[i]; p.Bs[i] = a->B_stride[i]; p.Cs[i] = a->C_stride[i];

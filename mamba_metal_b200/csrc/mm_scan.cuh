@@ -57,6 +57,7 @@ struct Params {
   const void* Cm;
   const float* A;
   const float* D;
+  const float* dbias;  // per-channel delta bias (added before softplus), or null
   float* state_out;
   long long us[3], ds[3], zs[3], ys[3], Bs[3], Cs[3], As[2];
   int batch, dim, nstate, seqlen;
@@ -251,7 +252,7 @@ constexpr float kMaxExpZ = 1.8446744e19f;      // 2^64: clamp of e^-z (SiLU of z
 template <typename T, int NM, bool SP, bool WY, bool ST, bool FULL>
 MM_DEV void compute_half(const uint4& tu, const uint4& td, const uint4& tz, const float* __restrict__ sB,
                          const float* __restrict__ sC, int kb, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
-                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, float& s_prev, bool has_z,
+                         float A0, float Dv, float Db, int nsteps, float& sum_d2, float& min_d2, float& s_prev, bool has_z,
                          float (&yk)[Stage<T, NM>::HT]) {
   constexpr int HT = Stage<T, NM>::HT;
   constexpr int HP = HT / 2;
@@ -269,7 +270,8 @@ MM_DEV void compute_half(const uint4& tu, const uint4& td, const uint4& tz, cons
     const float2 xf = vec_pair<T>(tu, kp);
     const float2 df = vec_pair<T>(td, kp);
     const f2_t x2 = f2_pack(xf.x, xf.y);
-    f2_t d2 = SP ? softplus_log2_2(f2_pack(df.x, df.y)) : f2_mul(f2_pack(df.x, df.y), f2_pack(kLog2e, kLog2e));
+    const f2_t draw = f2_add(f2_pack(df.x, df.y), f2_pack(Db, Db));  // + delta bias (0 without one)
+    f2_t d2 = SP ? softplus_log2_2(draw) : f2_mul(draw, f2_pack(kLog2e, kLog2e));
     const bool live0 = FULL || 2 * kp < nsteps;
     const bool live1 = FULL || 2 * kp + 1 < nsteps;
     if (!FULL) {
@@ -400,7 +402,7 @@ MM_DEV void compute_half(const uint4& tu, const uint4& td, const uint4& tz, cons
 // One staged tile = two half tiles. A full tile (the common case) is one branch-free block.
 template <typename T, int NM, bool SP, bool WY, bool ST, bool FULLTILE>
 MM_DEV void compute_tile_t(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
-                           float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, float& s_prev,
+                           float A0, float Dv, float Db, int nsteps, float& sum_d2, float& min_d2, float& s_prev,
                            const Lane<T>& ln, const Params& p, int t0, int lane) {
   constexpr int HT = Stage<T, NM>::HT;
   const float* sB = sm.bc;
@@ -415,10 +417,10 @@ MM_DEV void compute_tile_t(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2
     uint4 tz = make_uint4(0, 0, 0, 0);
     if (WY && p.has_z) tz = sm.io[slot][2][lane][v];
     if (FULLTILE || ns >= HT)
-      compute_half<T, NM, SP, WY, ST, true>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, HT, sum_d2, min_d2, s_prev,
+      compute_half<T, NM, SP, WY, ST, true>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, Db, HT, sum_d2, min_d2, s_prev,
                                            p.has_z, yk[v]);
     else
-      compute_half<T, NM, SP, WY, ST, false>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, ns, sum_d2, min_d2, s_prev,
+      compute_half<T, NM, SP, WY, ST, false>(tu, td, tz, sB, sC, v * HT, h, A2, A0, Dv, Db, ns, sum_d2, min_d2, s_prev,
                                             p.has_z, yk[v]);
   }
   if (WY && ln.active) {
@@ -443,13 +445,13 @@ MM_DEV void compute_tile_t(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2
 
 template <typename T, int NM, bool SP, bool WY, bool ST>
 MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2], const f2_t (&A2)[NM / 2],
-                         float A0, float Dv, int nsteps, float& sum_d2, float& min_d2, float& s_prev,
+                         float A0, float Dv, float Db, int nsteps, float& sum_d2, float& min_d2, float& s_prev,
                          const Lane<T>& ln, const Params& p, int t0, int lane) {
   if (nsteps == Stage<T, NM>::TT)
-    compute_tile_t<T, NM, SP, WY, ST, true>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, s_prev, ln, p, t0,
+    compute_tile_t<T, NM, SP, WY, ST, true>(sm, slot, h, A2, A0, Dv, Db, nsteps, sum_d2, min_d2, s_prev, ln, p, t0,
                                             lane);
   else
-    compute_tile_t<T, NM, SP, WY, ST, false>(sm, slot, h, A2, A0, Dv, nsteps, sum_d2, min_d2, s_prev, ln, p, t0,
+    compute_tile_t<T, NM, SP, WY, ST, false>(sm, slot, h, A2, A0, Dv, Db, nsteps, sum_d2, min_d2, s_prev, ln, p, t0,
                                              lane);
 }
 
@@ -460,7 +462,7 @@ MM_DEV void compute_tile(const WarpSmem<T, NM>& sm, int slot, f2_t (&h)[NM / 2],
 // `phases` holds the parity of each TMA ring slot's barrier and persists across calls.
 template <typename T, int NM, bool SP, bool WY, bool ST>
 MM_DEV int run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end, f2_t (&h)[NM / 2],
-                     const f2_t (&A2)[NM / 2], float A0, float Dv, float& sum_d2, float& min_d2,
+                     const f2_t (&A2)[NM / 2], float A0, float Dv, float Db, float& sum_d2, float& min_d2,
                      WarpSmem<T, NM>& sm, int lane, unsigned& phases, int stop_from = INT_MAX,
                      bool decays = false, float A_max = 0.f) {
   constexpr int TT = Stage<T, NM>::TT;
@@ -488,7 +490,7 @@ MM_DEV int run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end,
     convert_bc<T, NM>(sm, slot, lane);
     __syncwarp();
     const int t0 = t_begin + i * TT;
-    compute_tile<T, NM, SP, WY, ST>(sm, slot, h, A2, A0, Dv, min(TT, t_end - t0), sum_d2, min_d2, s_prev, ln, p, t0,
+    compute_tile<T, NM, SP, WY, ST>(sm, slot, h, A2, A0, Dv, Db, min(TT, t_end - t0), sum_d2, min_d2, s_prev, ln, p, t0,
                                     lane);
     __syncwarp();  // B/C buffer and this slot are free for the next iteration
     if (t0 + TT >= stop_from && t0 + TT < t_end &&
@@ -596,6 +598,7 @@ MM_DEV void process_piece(const Params& p, int w, int g, int tile_lo, int tile_h
   }
   const float A0 = A_row[0];
   const float Dv = p.has_D ? p.D[dd] : 0.f;
+  const float Db = p.dbias ? p.dbias[dd] : 0.f;
   float* so = (ln.active && p.state_out != nullptr) ? p.state_out + ((long long)ln.b * p.dim + ln.d) * p.nstate
                                                     : nullptr;
 
@@ -611,7 +614,7 @@ MM_DEV void process_piece(const Params& p, int w, int g, int tile_lo, int tile_h
   float acc = 0.f, min_d2 = INFINITY;
 
   // Pass 1 over the head: state only (its y is produced by the exact recompute below).
-  run_range<T, NM, SP, false, ST>(p, ln, t_lo, head_end, h, A2, A0, Dv, acc, min_d2, sm, lane, phases);
+  run_range<T, NM, SP, false, ST>(p, ln, t_lo, head_end, h, A2, A0, Dv, Db, acc, min_d2, sm, lane, phases);
 
   // Then one loop over the y-producing ranges: the rest of pass 1, and (for pieces that start
   // mid-sequence) the recompute from the true incoming state once the look-back has produced it.
@@ -621,7 +624,7 @@ MM_DEV void process_piece(const Params& p, int w, int g, int tile_lo, int tile_h
   const bool decays = A_max < 0.f;
   for (;;) {
     const int t_end_reached =
-        run_range<T, NM, SP, true, ST>(p, ln, t, t_hi, h, A2, A0, Dv, acc, min_d2, sm, lane, phases,
+        run_range<T, NM, SP, true, ST>(p, ln, t, t_hi, h, A2, A0, Dv, Db, acc, min_d2, sm, lane, phases,
                                        recompute ? head_end : INT_MAX,
                                        decays && (SP || min_d2 >= 0.f), A_max);
     if (recompute) {

@@ -5,8 +5,11 @@ dt_proj -> selective scan with A = -exp(A_log), D, z gate and softplus -> out_pr
 constructor, ``__call__`` / ``prefill`` / ``step`` and HF parameter names (in_proj, conv1d, x_proj,
 dt_proj, A_log, D, out_proj). Differences, all deliberate:
 
-- Activations stay channels-last (batch, seqlen, channels) end to end: the conv and scan kernels read
-  and write strided views, so the four transposes of mamba_block.py:90-100 do not exist here.
+- The parallel pass (forward / prefill) lays activations out as (channels, tokens): every projection is
+  one GEMM over all tokens whose output rows are channels, so the conv and the scan read t-contiguous
+  rows and the four transposes of mamba_block.py:90-100 do not exist here; dt_proj's bias is applied
+  inside the scan. Sequence lengths whose rows would not be 16-byte aligned use (tokens, channels)
+  strided views instead.
 - ``conv1d.weight`` has PyTorch/HF's (d_inner, 1, d_conv) layout (the reference transposes HF weights
   to MLX's (d_inner, d_conv, 1) at load_hf.py:46-50).
 - ``step`` returns new state tensors like the reference by default; ``step(..., inplace=True)``
@@ -102,6 +105,48 @@ class MambaBlock(nn.Module):
         return self._dt_bias_cache[1]
 
     def _run(self, x: torch.Tensor, want_state: bool):
+        bsz, L, _ = x.shape
+        es = torch.tensor([], dtype=self.in_proj.weight.dtype).element_size()
+        if (L * es) % 16 == 0:
+            return self._run_channel_first(x, want_state)
+        return self._run_channels_last(x, want_state)
+
+    def _run_channel_first(self, x: torch.Tensor, want_state: bool):
+        """Parallel pass with every activation laid out (channels, tokens): each projection is one GEMM over
+        all B*L tokens whose output rows are channels, so the conv and the scan read and write
+        t-contiguous rows (the scan's TMA path) and no transpose is materialised. dt_proj's bias is added
+        inside the scan (delta_bias)."""
+        bsz, L, D = x.shape
+        E, N, R = self.d_inner, self.d_state, self.dt_rank
+        dt_ = self.in_proj.weight.dtype
+        T = bsz * L
+        cf = lambda m, c: m.view(c, bsz, L).permute(1, 0, 2)                # (c, B*L) -> (B, c, L) view
+        xz_t = torch.matmul(self.in_proj.weight, x.to(dt_).reshape(T, D).t())  # (2E, B*L)
+        xc_t = torch.empty((E, T), dtype=dt_, device=x.device)
+        conv_state = torch.empty((bsz, E, self.d_conv), dtype=torch.float32, device=x.device) if want_state else None
+        ops.causal_conv1d(cf(xz_t[:E], E), self.conv1d.weight, self.conv1d.bias, silu=True, out=cf(xc_t, E),
+                          conv_state_out=conv_state)
+        xdbl_t = self._project_t(self.x_proj.weight, xc_t, 0)               # (R + 2N, B*L)
+        dt_t = torch.matmul(self.dt_proj.weight, xdbl_t[:R])                # (E, B*L), bias added in the scan
+        y_t = torch.empty((E, T), dtype=dt_, device=x.device)
+        ssm_state = torch.empty((bsz, E, N), dtype=torch.float32, device=x.device) if want_state else None
+        Df = self.D if self.D.dtype == torch.float32 else self.D.float()
+        selective_scan_into(cf(xc_t, E), cf(dt_t, E), self._A(), cf(xdbl_t[R:R + N], N), cf(xdbl_t[R + N:], N),
+                            Df, cf(xz_t[E:], E), cf(y_t, E), ssm_state, delta_softplus=True,
+                            delta_bias=self._dt_bias32())
+        out = self._project(y_t.t(), self.out_proj.weight, 1)             # (B*L, d_model)
+        return out.view(bsz, L, -1), conv_state, ssm_state
+
+    def _project_t(self, w: torch.Tensor, x_t: torch.Tensor, site: int) -> torch.Tensor:
+        """w @ x_t for a (K, tokens) activation -> (out_features, tokens); all-reduced over the group for a
+        tensor-parallel block (row-parallel x_proj)."""
+        if self.tp_reduce is None:
+            return torch.matmul(w, x_t)
+        return self.tp_reduce.transposed(w, x_t, self.tp_sites[site])
+
+    def _run_channels_last(self, x: torch.Tensor, want_state: bool):
+        """Parallel pass on (B, L, channels) activations, for sequence lengths whose channel-first rows
+        would not be 16-byte aligned: the conv and the scan read strided views of the GEMM outputs."""
         bsz, L, _ = x.shape
         E, N, R = self.d_inner, self.d_state, self.dt_rank
         dt_ = self.in_proj.weight.dtype

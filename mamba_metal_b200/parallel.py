@@ -77,6 +77,12 @@ class _TPProject:
         dist.all_reduce(t32, group=self.group)
         return t32.to(x.dtype)
 
+    def transposed(self, w: torch.Tensor, x_t: torch.Tensor, site: int) -> torch.Tensor:
+        """w @ x_t for a (K, tokens) activation (the channel-first prefill), all-reduced by NCCL in float32."""
+        t32 = torch.matmul(w, x_t).float()
+        dist.all_reduce(t32, group=self.group)
+        return t32.to(x_t.dtype)
+
     def partial(self, x: torch.Tensor, w: torch.Tensor, site: int):
         """Writes this rank's x @ w.T into the site's peer slot and returns a _PendingReduce whose
         add_rmsnorm finishes the all-reduce fused with the next residual add + RMSNorm; None when the

@@ -28,16 +28,17 @@ def _scan_dtype(*ts) -> torch.dtype:
 
 
 def selective_scan_into(u, delta, A, B, C, D, z, y, state_out, delta_softplus: bool, piece_tiles: int = 0,
-                        use_tma: bool = True):
+                        use_tma: bool = True, delta_bias=None):
     """Runs the scan kernel on given (possibly strided) views and writes into ``y`` / ``state_out``.
 
     u, delta, z, y: (batch, dim, seqlen) views with any strides (channel-first and channels-last both
     work); B, C: (batch, dstate, seqlen) views; A: (dim, dstate) float32; D: (dim,) float32 or None;
     state_out: contiguous float32 (batch, dim, dstate) or None. All activation views share one dtype.
     ``piece_tiles`` (0 = automatic) sets the timestep tiles per warp; ``use_tma=False`` stages tiles with
-    cp.async / plain loads even where TMA applies. Returns the workspace tensor (for status queries).
+    cp.async / plain loads even where TMA applies. ``delta_bias`` (dim,) float32, optional, is added to
+    delta before softplus (a Mamba block's dt_proj bias). Returns the workspace tensor (for status queries).
     """
-    dev = _lib.require_cuda(u, delta, A, B, C, D, z, y, state_out)
+    dev = _lib.require_cuda(u, delta, A, B, C, D, z, y, state_out, delta_bias)
     lib = _lib.lib()
     batch, dim, seqlen = u.shape
     dstate = A.shape[1]
@@ -56,6 +57,9 @@ def selective_scan_into(u, delta, A, B, C, D, z, y, state_out, delta_softplus: b
     args.delta_softplus = int(bool(delta_softplus))
     args.piece_tiles = int(piece_tiles)
     args.options = 0 if use_tma else 1
+    if delta_bias is not None:
+        assert delta_bias.dtype == torch.float32 and delta_bias.is_contiguous() and delta_bias.numel() == dim
+    args.delta_bias = _lib.ptr(delta_bias)
     nbytes = ctypes.c_size_t(0)
     _lib.check(lib.mm_selective_scan_workspace_size(ctypes.byref(args), ctypes.byref(nbytes)),
                "mm_selective_scan_workspace_size")

@@ -285,3 +285,31 @@ def test_exp2_poly_accuracy():
     em = ((ym.cpu().double() - exact).abs() / exact).max().item()
     print(f"exp2 max relative error: polynomial {ep:.3g}, ex2.approx {em:.3g}")
     assert ep <= 2.5e-7 and ep <= 2 * max(em, 1.2e-7)
+
+
+@pytest.mark.parametrize("use_tma", [True, False])
+def test_delta_bias_equals_biased_delta(use_tma):
+    """delta_bias (a Mamba block's dt_proj bias, added inside the scan before softplus) gives bit-identical
+    outputs to passing delta + bias (added in float32 beforehand), and both match the oracle. The layout
+    is the model's channel-first prefill one: (B, c, L) views of (c, B*L) buffers."""
+    b, d, n, L = 3, 80, 16, 520
+    inp = R.make_baseline_inputs(b, d, n, L, seed=21)
+    bias = np.random.default_rng(5).normal(size=(d,)).astype(np.float32) - 3.0
+    cf = lambda a: T(np.ascontiguousarray(np.transpose(a, (1, 0, 2))).reshape(a.shape[1], -1)).view(
+        a.shape[1], b, L).permute(1, 0, 2)
+    u, de, z, Bm, Cm = (cf(inp[k]) for k in ("u", "delta", "z", "B", "C"))
+    de_b = cf(inp["delta"] + bias[None, :, None])
+    outs = []
+    for delta, db in ((de, T(bias)), (de_b, None)):
+        y = torch.empty((d, b * L), device=DEV).view(d, b, L).permute(1, 0, 2)
+        h = torch.empty((b, d, n), device=DEV)
+        selective_scan_into(u, delta, T(inp["A"]), Bm, Cm, T(inp["D"]), z, y, h, True, use_tma=use_tma,
+                            delta_bias=db)
+        outs.append((y, h))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    q = dict(inp)
+    q["delta"] = inp["delta"] + bias[None, :, None]
+    yr, hr = R.selective_scan_vec(**q, delta_softplus=True, return_state=True, dtype=np.float64)
+    assert_close(outs[0][0], yr, RTOL["float32"], "delta_bias y")
+    assert_close(outs[0][1], hr, RTOL["float32"], "delta_bias state")
