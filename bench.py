@@ -785,7 +785,9 @@ def run_prefill(args, rank, world, local_rank):
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
+        torch.cuda.nvtx.range_push("timed_prefill3")  # ncu --nvtx --nvtx-include "timed_prefill3/"
         m3.prefill(ids3, last_only=True)
+        torch.cuda.nvtx.range_pop()
         e1.record(stream)
         torch.cuda.synchronize(dev)
         _, st3, ws3 = scan_stats_during(lambda: m3.prefill(ids3, last_only=True))
