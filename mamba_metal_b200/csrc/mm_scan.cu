@@ -93,9 +93,11 @@ static int make_plan(const MMScanArgs* a, Plan* pl) {
   if (a->piece_tiles > 0) {
     tpw = a->piece_tiles;
   } else {
-    // Fill the resident warp slots, but keep pieces long enough that the recomputed head
-    // (kHeadSteps) stays a small fraction of the work.
-    const long long min_tiles = std::max<long long>(1, (8 * kHeadSteps) / pl->TT);
+    // Fill the resident warp slots. A piece that starts mid-sequence recomputes at least its head
+    // (kHeadSteps) once the carry arrives, so its time is about P + min(P, R) steps for piece length P
+    // and decay length R; with the slots full, a longer P only adds time, so pieces are as short as the
+    // slots allow, down to two heads (below that the look-back and ring fill per piece dominate).
+    const long long min_tiles = std::max<long long>(1, (2 * kHeadSteps) / pl->TT);
     const long long want = resident_warps();
     tpw = std::max<long long>(min_tiles, (pl->total_tiles + want - 1) / want);
     // With at least as many (batch, channel group) rows as warp slots, whole rows per warp need no carry

@@ -290,8 +290,10 @@ def test_exp2_poly_accuracy():
 @pytest.mark.parametrize("use_tma", [True, False])
 def test_delta_bias_equals_biased_delta(use_tma):
     """delta_bias (a Mamba block's dt_proj bias, added inside the scan before softplus) gives bit-identical
-    outputs to passing delta + bias (added in float32 beforehand), and both match the oracle. The layout
-    is the model's channel-first prefill one: (B, c, L) views of (c, B*L) buffers."""
+    outputs to passing delta + bias (added in float32 beforehand) -- with one piece per row, so that no
+    carry hand-off is involved (the look-back may combine a predecessor's published prefix or walk its
+    aggregates, which round differently) -- and, with the library's own piece plan, matches the oracle.
+    The layout is the model's channel-first prefill one: (B, c, L) views of (c, B*L) buffers."""
     b, d, n, L = 3, 80, 16, 520
     inp = R.make_baseline_inputs(b, d, n, L, seed=21)
     bias = np.random.default_rng(5).normal(size=(d,)).astype(np.float32) - 3.0
@@ -300,16 +302,18 @@ def test_delta_bias_equals_biased_delta(use_tma):
     u, de, z, Bm, Cm = (cf(inp[k]) for k in ("u", "delta", "z", "B", "C"))
     de_b = cf(inp["delta"] + bias[None, :, None])
     outs = []
-    for delta, db in ((de, T(bias)), (de_b, None)):
+    whole_rows = (L + 7) // 8  # fp32 tiles of 8 steps per row
+    for delta, db, pieces in ((de, T(bias), whole_rows), (de_b, None, whole_rows), (de, T(bias), 0)):
         y = torch.empty((d, b * L), device=DEV).view(d, b, L).permute(1, 0, 2)
         h = torch.empty((b, d, n), device=DEV)
         selective_scan_into(u, delta, T(inp["A"]), Bm, Cm, T(inp["D"]), z, y, h, True, use_tma=use_tma,
-                            delta_bias=db)
+                            delta_bias=db, piece_tiles=pieces)
         outs.append((y, h))
     torch.cuda.synchronize()
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
     q = dict(inp)
     q["delta"] = inp["delta"] + bias[None, :, None]
     yr, hr = R.selective_scan_vec(**q, delta_softplus=True, return_state=True, dtype=np.float64)
-    assert_close(outs[0][0], yr, RTOL["float32"], "delta_bias y")
-    assert_close(outs[0][1], hr, RTOL["float32"], "delta_bias state")
+    for y, h in (outs[0], outs[2]):
+        assert_close(y, yr, RTOL["float32"], "delta_bias y")
+        assert_close(h, hr, RTOL["float32"], "delta_bias state")
