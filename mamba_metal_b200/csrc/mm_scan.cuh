@@ -512,47 +512,103 @@ MM_DEV int run_range(const Params& p, const Lane<T>& ln, int t_begin, int t_end,
 }
 
 // Decoupled look-back: returns (in h_in) the true state entering the piece owned by warp `w`.
+// Predecessors are examined in windows of up to 32: lane l reads the flag of warp pred - l (one round of
+// reads covers the window, and rounds repeat, with a bounded back-off, until lane 0's predecessor is
+// ready). The run of ready predecessors is consumed in order up to the first inclusive prefix (flag 2);
+// flags beyond it are never waited on (a warp whose only piece ends its row publishes nothing). Aggregates
+// are read LB predecessors at a time so that their loads are in flight together. h_in = sum over the
+// consumed predecessors j of 2^(A * q_j) * state_j, q_j the summed delta2 between predecessor j's end and
+// this piece's start.
 template <int NM>
 MM_DEV void lookback(const Params& p, int w, int lane, const float (&Areg)[NM], float (&h_in)[NM]) {
+  constexpr int LB = NM <= 16 ? 2 : 1;  // predecessors whose state blocks are loaded together
 #pragma unroll
   for (int n = 0; n < NM; ++n) h_in[n] = 0.f;
   float qsum = 0.f;  // accumulated sum of delta2 between the predecessor's end and this piece's start
   int pred = w - 1;
   unsigned long long spins = 0, hops = 0;
-  while (pred >= 0) {
-    unsigned f = 0;
-    if (lane == 0) {
-      const unsigned* fp = p.flags + (long long)pred * kFlagStride;
+  bool done = false;
+  while (pred >= 0 && !done) {
+    const int W = min(32, pred + 1);
+    unsigned f = 0, ready = 0;
+    {
       unsigned ns = 32;
       unsigned long long t_start = 0;
-      while ((f = ld_relaxed(fp)) == 0u) {
-        if (t_start == 0) t_start = globaltimer_ns();
-        else if (globaltimer_ns() - t_start > kSpinLimitNs) {
-          atomicOr(p.err, 1u);
-          f = 3u;  // give up: treat as an empty prefix
+      for (;;) {
+        f = lane < W ? ld_relaxed(p.flags + (long long)(pred - lane) * kFlagStride) : 0u;
+        ready = __ballot_sync(0xffffffffu, f != 0u);
+        if (ready & 1u) break;
+        bool give_up = false;
+        if (lane == 0) {
+          if (t_start == 0) t_start = globaltimer_ns();
+          else give_up = globaltimer_ns() - t_start > kSpinLimitNs;
+          if (give_up) atomicOr(p.err, 1u);
+        }
+        if (__shfl_sync(0xffffffffu, give_up, 0)) {
+          done = true;  // treat the prefix as ended
           break;
         }
         __nanosleep(ns);
         ns = min(ns * 2, 1024u);
         ++spins;
       }
-      fence_acq_rel();  // acquire: the predecessor's data below is read after its flag
     }
-    f = __shfl_sync(0xffffffffu, f, 0);
-    if (f == 3u) break;
-    ++hops;
-    if (lane != 0) fence_acq_rel();
-    if (f == 2u) {
-      const float* src = p.pre + (long long)pred * NM * 32;
+    if (done) break;
+    fence_acq_rel();  // acquire: the predecessors' data below is read after their flags
+    const int run = (~ready) ? __ffs(~ready) - 1 : 32;  // consecutive ready predecessors from pred down
+    const unsigned pre_mask = __ballot_sync(0xffffffffu, lane < run && f == 2u);
+    const int last = pre_mask ? __ffs(pre_mask) - 1 : run - 1;  // consume pred .. pred - last
+    if constexpr (LB > 1) {
+      for (int j0 = 0; j0 <= last && !done; j0 += LB) {
+        float v[LB][NM + 1];
+        unsigned fj[LB];
 #pragma unroll
-      for (int n = 0; n < NM; ++n) h_in[n] += ex2(Areg[n] * qsum) * __ldcg(src + n * 32 + lane);
-      break;
+        for (int b = 0; b < LB; ++b) {
+          const int j = min(j0 + b, last);
+          fj[b] = __shfl_sync(0xffffffffu, f, j);
+          const int pj = pred - j;
+          const float* src = fj[b] == 2u ? p.pre + (long long)pj * NM * 32 : p.agg + (long long)pj * (NM + 1) * 32;
+#pragma unroll
+          for (int n = 0; n < NM; ++n) v[b][n] = fj[b] == 3u ? 0.f : __ldcg(src + n * 32 + lane);
+          v[b][NM] = fj[b] == 1u ? __ldcg(src + NM * 32 + lane) : 0.f;
+        }
+#pragma unroll
+        for (int b = 0; b < LB; ++b) {
+          if (j0 + b > last || done) break;
+          if (fj[b] == 3u) {
+            done = true;
+            break;
+          }
+          ++hops;
+#pragma unroll
+          for (int n = 0; n < NM; ++n) h_in[n] += ex2(Areg[n] * qsum) * v[b][n];
+          if (fj[b] == 2u) {
+            done = true;
+            break;
+          }
+          qsum += v[b][NM];
+        }
+      }
+    } else {
+      for (int j = 0; j <= last; ++j) {
+        const unsigned fj = __shfl_sync(0xffffffffu, f, j);
+        if (fj == 3u) {
+          done = true;
+          break;
+        }
+        ++hops;
+        const int pj = pred - j;
+        const float* src = fj == 2u ? p.pre + (long long)pj * NM * 32 : p.agg + (long long)pj * (NM + 1) * 32;
+#pragma unroll
+        for (int n = 0; n < NM; ++n) h_in[n] += ex2(Areg[n] * qsum) * __ldcg(src + n * 32 + lane);
+        if (fj == 2u) {
+          done = true;
+          break;
+        }
+        qsum += __ldcg(src + NM * 32 + lane);
+      }
     }
-    const float* src = p.agg + (long long)pred * (NM + 1) * 32;
-#pragma unroll
-    for (int n = 0; n < NM; ++n) h_in[n] += ex2(Areg[n] * qsum) * __ldcg(src + n * 32 + lane);
-    qsum += __ldcg(src + NM * 32 + lane);
-    --pred;
+    pred -= last + 1;
   }
   if (lane == 0) {
     atomicAdd(p.stats + 0, spins);
