@@ -178,6 +178,10 @@ typedef struct MMConvStepArgs {
   int64_t batch, dim, width;
   int64_t x_stride_b, out_stride_b;
   int64_t silu;
+  int64_t early_state; /* 1: conv_state was not written by the kernel just before this call on `stream`, so
+                          the call may start (and load the state) while that kernel finishes; everything
+                          else is read after it completes (programmatic dependent launch). 0: plain
+                          stream order */
 } MMConvStepArgs;
 
 int mm_causal_conv1d_step(const MMConvStepArgs* args, mm_stream_t stream);
@@ -205,6 +209,9 @@ typedef struct MMSSMStepArgs {
   int64_t batch, dim, dstate;
   int64_t x_stride_b, dt_stride_b, z_stride_b, B_stride_b, C_stride_b, y_stride_b;
   int64_t dt_softplus; /* 0 / 1 */
+  int64_t early_state; /* 1: ssm_state was not written by the kernel just before this call on `stream`, so
+                          the call may start (and stream the state in) while that kernel finishes; every
+                          other input is read after it completes (programmatic dependent launch) */
 } MMSSMStepArgs;
 
 int mm_ssm_decode_step(const MMSSMStepArgs* args, mm_stream_t stream);

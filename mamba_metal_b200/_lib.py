@@ -52,7 +52,7 @@ class MMConvStepArgs(ctypes.Structure):
     _fields_ = [
         ("x", _p), ("conv_state", _p), ("weight", _p), ("bias", _p), ("out", _p), ("dtype", _i64),
         ("batch", _i64), ("dim", _i64), ("width", _i64), ("x_stride_b", _i64), ("out_stride_b", _i64),
-        ("silu", _i64),
+        ("silu", _i64), ("early_state", _i64),
     ]
 
 
@@ -61,7 +61,7 @@ class MMSSMStepArgs(ctypes.Structure):
         ("x", _p), ("dt", _p), ("z", _p), ("B", _p), ("C", _p), ("A", _p), ("D", _p), ("ssm_state", _p),
         ("y", _p), ("dtype", _i64), ("batch", _i64), ("dim", _i64), ("dstate", _i64),
         ("x_stride_b", _i64), ("dt_stride_b", _i64), ("z_stride_b", _i64), ("B_stride_b", _i64),
-        ("C_stride_b", _i64), ("y_stride_b", _i64), ("dt_softplus", _i64),
+        ("C_stride_b", _i64), ("y_stride_b", _i64), ("dt_softplus", _i64), ("early_state", _i64),
     ]
 
 

@@ -255,6 +255,13 @@ MM_DEV void tma_load_3d(void* smem_dst, const CUtensorMap* tm, int x, int y, int
       : "memory");
 }
 
+// ---- Programmatic dependent launch -------------------------------------------------------------
+// Waits until the grid this launch depends on (the previous kernel in the stream, when launched with
+// programmatic stream serialization) has completed and its memory is visible; a no-op otherwise.
+MM_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the dependent launch of this grid start its own prologue.
+MM_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- Memory-model helpers for carry hand-off ----------------------------------------------------
 MM_DEV unsigned ld_acquire(const unsigned* p) {
   unsigned v;
@@ -274,6 +281,24 @@ MM_DEV unsigned long long globaltimer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// Launches kernel<<<grid, block, 0, s>>>(params); with early != 0 as a programmatic dependent launch (the
+// kernel may start while the previous kernel in the stream finishes; it calls grid_dep_wait before
+// reading anything that kernel produced).
+template <typename K, typename P>
+inline cudaError_t launch_maybe_early(K kernel, dim3 grid, dim3 block, cudaStream_t s, int64_t early, const P& params) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = early ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, params);
 }
 
 inline int dtype_size(int64_t dtype) {

@@ -342,10 +342,13 @@ __global__ void __launch_bounds__(256) conv_step_kernel(const StepParams p) {
   if (d >= p.dim) return;
   const long long i = (long long)b * p.dim + d;
   float4* st = reinterpret_cast<float4*>(p.state + i * kW);
+  // the window state first (with an early-state launch it loads while the kernel before this one
+  // finishes); everything else after grid_dep_wait
   const float4 s = *st;
-  const float xn = ld_f32(static_cast<const T*>(p.x) + b * p.xsb + d);
+  grid_dep_wait();
   const float4 w = *reinterpret_cast<const float4*>(p.w + d * kW);
   float v = p.bias ? p.bias[d] : 0.f;
+  const float xn = ld_f32(static_cast<const T*>(p.x) + b * p.xsb + d);
   v = fmaf(w.x, s.y, v);
   v = fmaf(w.y, s.z, v);
   v = fmaf(w.z, s.w, v);
@@ -400,8 +403,9 @@ extern "C" int mm_causal_conv1d_step(const MMConvStepArgs* a, mm_stream_t stream
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a->batch > 65535 || a->dim > (1 << 30)) return MM_ERR_SHAPE;  // grid.y = batch
   const dim3 blocks((unsigned)((p.dim + 255) / 256), (unsigned)p.batch);
-  if (a->dtype == MM_F32) conv::conv_step_kernel<float><<<blocks, 256, 0, s>>>(p);
-  else if (a->dtype == MM_F16) conv::conv_step_kernel<__half><<<blocks, 256, 0, s>>>(p);
-  else conv::conv_step_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(p);
-  return cudaGetLastError() == cudaSuccess ? MM_OK : MM_ERR_LAUNCH;
+  cudaError_t e;
+  if (a->dtype == MM_F32) e = launch_maybe_early(conv::conv_step_kernel<float>, blocks, 256, s, a->early_state, p);
+  else if (a->dtype == MM_F16) e = launch_maybe_early(conv::conv_step_kernel<__half>, blocks, 256, s, a->early_state, p);
+  else e = launch_maybe_early(conv::conv_step_kernel<__nv_bfloat16>, blocks, 256, s, a->early_state, p);
+  return e == cudaSuccess ? MM_OK : MM_ERR_LAUNCH;
 }

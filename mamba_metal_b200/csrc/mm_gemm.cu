@@ -87,8 +87,6 @@ MM_DEV uint64_t sw128_desc(const void* p) {
 MM_DEV void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
   asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
-MM_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-MM_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Waits for the phase of `bar` with the given parity: a short burst of polls, then polls bounded by time.
 MM_DEV bool wait_phase(unsigned long long* bar, unsigned parity) {
@@ -174,6 +172,9 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       tma_load_2d(s.w[i], &p.tm_w, (kb0 + i) * BK, n_tile * BM, &s.full[i]);
     }
     grid_dep_wait();
+    // Only now (the kernel before this one has completed) may the next kernel start its prologue: a
+    // dependent that reads its own inputs early then never overtakes a kernel two launches back.
+    grid_dep_launch();
     for (int i = 0; i < nkb; ++i) {
       const int st = i % kStages;
       if (i >= kStages && !wait_phase(&s.empty[st], ((i / kStages) & 1) ^ 1)) {
@@ -213,7 +214,6 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
   __syncwarp();
 
   // Epilogue: thread (warp w, lane l) owns output feature n_tile * 128 + 32 w + l for the 64 tokens.
-  grid_dep_launch();  // the next kernel may start its own prologue
   const bool got = wait_phase(&s.done, 0);
   tc_fence_after();
   const int nl = warp * 32 + lane;

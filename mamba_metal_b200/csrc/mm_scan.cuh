@@ -35,7 +35,10 @@ namespace scan {
 #define MM_SCAN_SUBTILE 4  // timesteps of one pass over the state pairs in the recurrence
 #endif
 #ifndef MM_SCAN_POLY_EIGHTHS
-#define MM_SCAN_POLY_EIGHTHS 3  // general A: eighths of the state pairs whose exp2 runs on the FMA pipe
+#define MM_SCAN_POLY_EIGHTHS 0  // general A: eighths of the state pairs whose exp2 runs as a polynomial on the
+                                // FMA pipe. Measured on B200 (configs[1], random A_log): 0 -> 382 us, 2 -> 427,
+                                // 3 -> 461, 4 -> 503, 6 -> 609: the kernel is bound by instruction issue, and a
+                                // polynomial costs more issue slots than the MUFU ex2 it replaces
 #endif
 #ifndef MM_SCAN_MIN_BLOCKS
 #define MM_SCAN_MIN_BLOCKS 3  // resident 4-warp CTAs per SM the dstate <= 16 kernels are compiled for: 3 (168

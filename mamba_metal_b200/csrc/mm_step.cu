@@ -78,8 +78,8 @@ __global__ void __launch_bounds__(128) ssm_step_kernel(const SSMParams p) {
 // dstate 16, dim a multiple of 8, 16-byte aligned rows: CTA = 32 channels x kQdGroups groups of kQdRows
 // batch rows, 128 threads; thread (dl, q) owns states 4q..4q+3 of channel d0 + dl, so a warp's
 // 16-byte state accesses are contiguous. At entry the CTA starts cp.async copies of both groups' state
-// rows and dt / x / z row slices (one commit group each; nothing held in registers), loads B | C with
-// plain loads, then computes group 0 while group 1 is still in flight.
+// rows (one commit group), then of each group's dt / x / z row slices (one commit group each; nothing held in
+// registers), loads B | C with plain loads, then computes group 0 while group 1 is still in flight.
 #ifndef MM_SSM_ROWS
 #define MM_SSM_ROWS 4  // batch rows per group in the dstate-16 decode step: 4 (1280 CTAs at batch 64)
                        // measured 10.1 us vs 12.2 us with 8 at the 2.8b decode shape
@@ -105,6 +105,9 @@ __global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMPara
   const int tid = threadIdx.x, dl = tid >> 2, q = tid & 3;
   const int d0 = blockIdx.x * kQdCh, d = d0 + dl;
   const bool dok = d < p.dim;
+  // State rows first: with an early-state launch (programmatic dependent launch) they stream in while the
+  // kernel before this one is still finishing; everything that kernel may have produced (dt, x, z, B, C)
+  // is read only after grid_dep_wait.
 #pragma unroll
   for (int g = 0; g < kQdGroups; ++g) {
     const int b0 = (blockIdx.y * kQdGroups + g) * kQdRows;
@@ -113,6 +116,15 @@ __global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMPara
     for (int r = 0; r < kQdRows; ++r)
       if (dok && r < nrows)
         cp_async16(&sm.h[g][r][tid], p.state + ((long long)(b0 + r) * p.dim + d) * 16 + 4 * q);
+  }
+  cp_async_commit();
+  grid_dep_wait();
+  const float4 a = dok ? *reinterpret_cast<const float4*>(p.A + (long long)d * 16 + 4 * q) : make_float4(0, 0, 0, 0);
+  const float Dd = (dok && p.D) ? p.D[d] : 0.f;
+#pragma unroll
+  for (int g = 0; g < kQdGroups; ++g) {
+    const int b0 = (blockIdx.y * kQdGroups + g) * kQdRows;
+    const int nrows = max(0, min(kQdRows, p.batch - b0));
     for (int i = tid; i < 3 * kQdRows * kChunks; i += kQdThreads) {
       const int a = i / (kQdRows * kChunks), rem = i - a * kQdRows * kChunks;
       const int r = rem / kChunks, c = (rem - r * kChunks) * VE;
@@ -133,11 +145,9 @@ __global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMPara
                     : ld_f32(static_cast<const T*>(p.C) + (long long)b * p.Csb + (lane - 16));
     sm.bc[g][r][lane] = v;
   }
-  const float4 a = dok ? *reinterpret_cast<const float4*>(p.A + (long long)d * 16 + 4 * q) : make_float4(0, 0, 0, 0);
-  const float Dd = (dok && p.D) ? p.D[d] : 0.f;
 #pragma unroll
   for (int g = 0; g < kQdGroups; ++g) {
-    if (g == 0) cp_async_wait<kQdGroups - 1>();
+    if (g == 0) cp_async_wait<kQdGroups - 1>();  // the state group and group 0's row slices
     else cp_async_wait<0>();
     __syncthreads();
     const int b0 = (blockIdx.y * kQdGroups + g) * kQdRows;
@@ -310,10 +320,11 @@ extern "C" int mm_ssm_decode_step(const MMSSMStepArgs* a, mm_stream_t stream) {
   if (p.vec && p.dim % 8 == 0 && rows16) {
     const int rows_per_cta = step::kQdRows * step::kQdGroups;
     const dim3 qgrid((p.dim + step::kQdCh - 1) / step::kQdCh, (p.batch + rows_per_cta - 1) / rows_per_cta);
-    if (a->dtype == MM_F32) step::ssm_step_quad_kernel<float><<<qgrid, step::kQdThreads, 0, s>>>(p);
-    else if (a->dtype == MM_F16) step::ssm_step_quad_kernel<__half><<<qgrid, step::kQdThreads, 0, s>>>(p);
-    else step::ssm_step_quad_kernel<__nv_bfloat16><<<qgrid, step::kQdThreads, 0, s>>>(p);
-    return cudaGetLastError() == cudaSuccess ? MM_OK : MM_ERR_LAUNCH;
+    cudaError_t e;
+    if (a->dtype == MM_F32) e = launch_maybe_early(step::ssm_step_quad_kernel<float>, qgrid, step::kQdThreads, s, a->early_state, p);
+    else if (a->dtype == MM_F16) e = launch_maybe_early(step::ssm_step_quad_kernel<__half>, qgrid, step::kQdThreads, s, a->early_state, p);
+    else e = launch_maybe_early(step::ssm_step_quad_kernel<__nv_bfloat16>, qgrid, step::kQdThreads, s, a->early_state, p);
+    return e == cudaSuccess ? MM_OK : MM_ERR_LAUNCH;
   }
   const dim3 grid((p.dim + 127) / 128, p.batch);
   // the NM = 16 instantiation handles any dstate through its scalar branch when not vectorisable

@@ -191,12 +191,15 @@ class MambaBlock(nn.Module):
         if not inplace or ssm_state.dtype != torch.float32 or not ssm_state.is_contiguous():
             ssm_state = ssm_state.to(torch.float32, copy=True).contiguous()
         xz = decode_linear(x_token[:, 0].to(dt_), self.in_proj.weight)  # (B, 2E)
-        xc = ops.causal_conv1d_step(xz[:, :E], conv_state, self.conv1d.weight, self.conv1d.bias, silu=True)
+        # early_state: the kernel just before each of the two step kernels is a projection GEMM, which does
+        # not write the state they update, so they may start loading it while the GEMM finishes
+        xc = ops.causal_conv1d_step(xz[:, :E], conv_state, self.conv1d.weight, self.conv1d.bias, silu=True,
+                                    early_state=True)
         x_dbl = self._project(xc, self.x_proj.weight, 0)                    # (B, R + 2N)
         Df = self.D if self.D.dtype == torch.float32 else self.D.float()
         dt = decode_linear(x_dbl[:, :R], self.dt_proj.weight, self.dt_proj.bias, bias32=self._dt_bias32())
         y = ops.ssm_decode_step(xc, dt, xz[:, E:], x_dbl[:, R:R + N], x_dbl[:, R + N:], self._A(), Df,
-                                ssm_state, dt_softplus=True)
+                                ssm_state, dt_softplus=True, early_state=True)
         if defer_out and self.tp_reduce is not None and hasattr(self.tp_reduce, "partial"):
             # tensor parallel: leave out_proj's all-reduce to the caller's fused residual add + RMSNorm
             pending = self.tp_reduce.partial(y, self.out_proj.weight, self.tp_sites[1])

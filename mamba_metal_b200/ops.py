@@ -55,10 +55,12 @@ def causal_conv1d(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | No
 
 
 def causal_conv1d_step(x: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
-                       *, silu: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
+                       *, silu: bool = True, out: torch.Tensor | None = None, early_state: bool = False) -> torch.Tensor:
     """One decode step of the conv, updating ``conv_state`` (float32 (batch, dim, 4), contiguous) in
     place: window shift + append, dot with the weight, + bias, SiLU (mamba_block.py:171-177).
-    x: (batch, dim) with unit inner stride (row stride free). Returns out (batch, dim) of x.dtype."""
+    x: (batch, dim) with unit inner stride (row stride free). Returns out (batch, dim) of x.dtype.
+    ``early_state``: the caller guarantees that the kernel issued just before this call did not write
+    ``conv_state``; the step then starts loading the state while that kernel finishes."""
     batch, dim = x.shape
     assert x.stride(1) == 1
     assert conv_state.is_contiguous() and conv_state.dtype == torch.float32
@@ -76,16 +78,20 @@ def causal_conv1d_step(x: torch.Tensor, conv_state: torch.Tensor, weight: torch.
     a.batch, a.dim, a.width = batch, dim, D_CONV
     a.x_stride_b, a.out_stride_b = x.stride(0), out.stride(0)
     a.silu = int(bool(silu))
+    a.early_state = int(bool(early_state))
     with torch.cuda.device(dev):
         rc = _lib.lib().mm_causal_conv1d_step(ctypes.byref(a), _lib.stream_handle(dev))
     _lib.check(rc, "mm_causal_conv1d_step")
     return out
 
 
-def ssm_decode_step(x, dt, z, B, C, A, D, ssm_state, *, dt_softplus: bool = True, out=None) -> torch.Tensor:
+def ssm_decode_step(x, dt, z, B, C, A, D, ssm_state, *, dt_softplus: bool = True, out=None,
+                    early_state: bool = False) -> torch.Tensor:
     """One decode step of the SSM, updating ``ssm_state`` (float32 (batch, dim, dstate), contiguous) in
     place (mamba_block.py:183-195). x, dt, z: (batch, dim); B, C: (batch, dstate) (row strides free,
-    unit inner stride); A: (dim, dstate) float32 contiguous; D: (dim,) float32 or None."""
+    unit inner stride); A: (dim, dstate) float32 contiguous; D: (dim,) float32 or None.
+    ``early_state``: the caller guarantees that the kernel issued just before this call did not write
+    ``ssm_state``; the step then streams the state in while that kernel finishes."""
     batch, dim = x.shape
     dstate = A.shape[1]
     for t in (x, dt, z, B, C):
@@ -105,6 +111,7 @@ def ssm_decode_step(x, dt, z, B, C, A, D, ssm_state, *, dt_softplus: bool = True
     a.z_stride_b = z.stride(0) if z is not None else 0
     a.B_stride_b, a.C_stride_b, a.y_stride_b = B.stride(0), C.stride(0), out.stride(0)
     a.dt_softplus = int(bool(dt_softplus))
+    a.early_state = int(bool(early_state))
     with torch.cuda.device(dev):
         rc = _lib.lib().mm_ssm_decode_step(ctypes.byref(a), _lib.stream_handle(dev))
     _lib.check(rc, "mm_ssm_decode_step")

@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
 def test_struct_layouts_are_padding_free():
     # all fields are 8 bytes wide, so sizeof == 8 * field count on every FFI
     for s, n in ((_lib.MMScanArgs, 9 + 5 + 6 * 3 + 2 + 3 + 1), (_lib.MMConvArgs, 5 + 4 + 1 + 6 + 1),
-                 (_lib.MMConvStepArgs, 5 + 1 + 3 + 2 + 1), (_lib.MMSSMStepArgs, 9 + 1 + 3 + 6 + 1),
+                 (_lib.MMConvStepArgs, 5 + 1 + 3 + 2 + 1 + 1), (_lib.MMSSMStepArgs, 9 + 1 + 3 + 6 + 1 + 1),
                  (_lib.MMAddNormArgs, 4 + 1 + 2 + 2 + 1)):
         assert ctypes.sizeof(s) == 8 * n, s.__name__
 
