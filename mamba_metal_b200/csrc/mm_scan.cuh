@@ -106,7 +106,7 @@ template <typename T, int NM> struct __align__(128) WarpSmem {
   uint4 io[kStages][3][32][2];       // [stage][u, delta, z][row = lane][two 16-byte vectors]
   uint4 bcraw[kStages][2 * NM][2];   // [stage][B rows, then C rows][two vectors]
   unsigned long long bar[kStages];   // TMA completion barriers
-  float bc[Stage<T, NM>::BCF];
+  __align__(16) float bc[Stage<T, NM>::BCF];  // read as float4: 16-byte aligned whatever kStages is
 };
 
 // Per-piece context of one lane.
