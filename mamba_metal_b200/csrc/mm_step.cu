@@ -81,8 +81,9 @@ __global__ void __launch_bounds__(128) ssm_step_kernel(const SSMParams p) {
 // rows (one commit group), then of each group's dt / x / z row slices (one commit group each; nothing held in
 // registers), loads B | C with plain loads, then computes group 0 while group 1 is still in flight.
 #ifndef MM_SSM_ROWS
-#define MM_SSM_ROWS 4  // batch rows per group in the dstate-16 decode step: 4 (1280 CTAs at batch 64)
-                       // measured 10.1 us vs 12.2 us with 8 at the 2.8b decode shape
+#define MM_SSM_ROWS 2  // batch rows per group in the dstate-16 decode step. At the 2.8b decode shape (batch 64,
+                       // 5120 channels, CUDA graph, states beyond L2) rows x groups measured: 2 x 2 8.7 us,
+                       // 4 x 1 8.7, 1 x 4 9.2, 4 x 2 9.7, 8 x 1 9.7, 4 x 4 12.0 us
 #endif
 #ifndef MM_SSM_GROUPS
 #define MM_SSM_GROUPS 2  // row groups per CTA (copies of later groups overlap earlier groups' compute)
