@@ -106,3 +106,35 @@ def test_add_rmsnorm(dtype, rows, dim):
     ref = R.rmsnorm_ref(ref_res.numpy(), w.numpy(), 1e-5)
     assert_close(r, ref_res, 1e-6, "residual")
     assert_close(out, ref, RTOL[name(dtype)], "norm")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_early_state_launch_is_bit_identical(dtype):
+    """early_state=True (programmatic dependent launch: the state is loaded while the preceding kernel,
+    here a GEMM that does not touch the state, finishes) gives bit-identical outputs and states to the
+    plain stream-ordered launch, over a chain of steps each preceded by the GEMM producing its input."""
+    g = torch.Generator(device="cuda:0").manual_seed(3)
+    b, d, n = 64, 1024, 16
+    dev = "cuda:0"
+    w_in = (torch.randn((2 * d, 256), generator=g, device=dev) * 0.05).to(dtype)
+    xs = [torch.randn((b, 256), generator=g, device=dev).to(dtype) for _ in range(6)]
+    cw = torch.randn((d, 4), generator=g, device=dev) * 0.3
+    cb = torch.randn((d,), generator=g, device=dev) * 0.1
+    A = -torch.rand((d, n), generator=g, device=dev) - 0.2
+    D = torch.randn((d,), generator=g, device=dev)
+    Bm = torch.randn((b, n), generator=g, device=dev).to(dtype)
+    Cm = torch.randn((b, n), generator=g, device=dev).to(dtype)
+    outs = {}
+    for early in (False, True):
+        conv = torch.zeros((b, d, 4), device=dev)
+        ssm = torch.zeros((b, d, n), device=dev)
+        ys = []
+        for x in xs:
+            xz = x @ w_in.T                      # the kernel just before the conv step
+            xc = causal_conv1d_step(xz[:, :d], conv, cw, cb, silu=True, early_state=early)
+            dt = xz[:, :d] @ torch.eye(d, device=dev, dtype=dtype)  # a GEMM just before the SSM step
+            ys.append(ssm_decode_step(xc, dt, xz[:, d:], Bm, Cm, A, D, ssm, early_state=early))
+        torch.cuda.synchronize()
+        outs[early] = (torch.stack(ys), conv.clone(), ssm.clone())
+    for a, c in zip(outs[False], outs[True]):
+        assert torch.equal(a, c)
