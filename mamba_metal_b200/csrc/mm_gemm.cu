@@ -23,6 +23,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "mm_common.cuh"
 
@@ -322,16 +323,18 @@ struct Plan {
   size_t ws_bytes, partial_off;
 };
 
+// SM count of the current device, cached per device in atomics: concurrent first calls may both query it,
+// and both store the same value.
 static int sm_count() {
-  static int cached[64] = {};
+  static std::atomic<int> cached[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int v = 148;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = v;
-  }
-  return cached[dev];
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  v = 148;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  cached[dev].store(v, std::memory_order_relaxed);
+  return v;
 }
 
 static int make_plan(const MMLinearArgs* a, Plan* pl) {

@@ -106,8 +106,7 @@ class MambaBlock(nn.Module):
 
     def _run(self, x: torch.Tensor, want_state: bool):
         bsz, L, _ = x.shape
-        es = torch.tensor([], dtype=self.in_proj.weight.dtype).element_size()
-        if (L * es) % 16 == 0:
+        if (L * self.in_proj.weight.dtype.itemsize) % 16 == 0:
             return self._run_channel_first(x, want_state)
         return self._run_channels_last(x, want_state)
 
