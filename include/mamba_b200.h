@@ -303,8 +303,9 @@ int mm_exp2_check(const float* x, float* y_poly, float* y_mufu, int64_t n, mm_st
  * Replaces the nn.Linear calls of the decode step, mamba_metal/mamba_block.py:167 (in_proj), :179
  * (x_proj), :181 (dt_proj) and :197 (out_proj); the same shapes serve any small-M product. Base
  * pointers and row strides of x and w must be 16-byte aligned (TMA). splits = 0 lets the library split
- * K over CTAs so that every SM streams weights; split partials are summed in a fixed order by the last
- * CTA of each output tile, so the result does not depend on scheduling. The workspace (size from
+ * K over CTAs so that every SM streams weights; split partials are added into an fp32 tile of the
+ * workspace in arrival order, so with splits > 1 results can differ in the last bits between calls.
+ * The workspace (size from
  * mm_linear_workspace_size, 256-byte aligned) must be zero-filled before its first use; every call
  * leaves it zeroed again. Calls sharing a workspace must not overlap on the GPU.
  * ------------------------------------------------------------------------------------------- */

@@ -7,13 +7,14 @@
 //   - the tile is swapped: the MMA's M side is 128 output features (rows of W), its N side the batch
 //     (64 tokens), so one tcgen05.mma.cta_group::1.kind::f16 (M 128, N 64, K 16, bf16 in, fp32 out)
 //     consumes a 128 x 16 slab of W and the whole batch;
-//   - W and x tiles arrive by TMA (128-byte swizzled rows, no multicast) into a 6-stage ring (144 KB, one
-//     CTA per SM, at most one wave of CTAs); one elected thread issues the TMA copies, another the MMAs;
+//   - W and x tiles arrive by TMA (128-byte swizzled rows, no multicast) into a 4-stage ring (96 KB, two
+//     CTAs per SM, at most one wave of CTAs); one elected thread issues the TMA copies, another the MMAs;
 //     accumulators live in TMEM (64 columns);
 //   - the K range is split over CTAs so that every SM streams weight bytes even when N / 128 is small
-//     (out_proj: 2560 / 128 = 20 tiles); split partials are reduced by the last CTA of each tile to
-//     arrive (a per-tile counter), in split order, so results do not depend on arrival order and no
-//     output buffer has to be zeroed. The last CTA adds the bias and writes fp32 or bf16;
+//     (out_proj: 2560 / 128 = 20 tiles); each split adds its partial into an fp32 tile of the workspace
+//     with vector reductions (red.global.add.v4.f32), and the last CTA of the tile to arrive (a per-tile
+//     counter) reads the sum once, adds the bias, writes fp32 or bf16 and zeroes the tile again. The order
+//     of the fp32 additions follows arrival, so split results can differ in the last bits between calls;
 //   - the launch is a programmatic dependent launch: a CTA initialises its barriers and TMEM, prefetches
 //     its tensor maps and starts the copies of its first weight stages (weights are constants of the
 //     step) while the kernel before it in the stream is still finishing, and waits for that kernel
@@ -33,12 +34,13 @@ namespace gemm {
 constexpr int BM = 128;  // output features per CTA (MMA M)
 constexpr int BN = 64;   // tokens per CTA (MMA N)
 constexpr int BK = 64;   // K elements per stage: one 128-byte swizzle row of bf16
-constexpr int kStages = 6;
+constexpr int kStages = 4;
 constexpr int kThreads = 128;
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 constexpr unsigned kTmemCols = 64;  // BN fp32 accumulator columns
 constexpr int kMaxTiles = 4096;     // output tiles with a split counter (larger calls run unsplit)
-constexpr int kMaxSplits = 16;     // the last CTA of a tile reads every split's partial: keep that short
+constexpr int kMaxSplits = 16;
+constexpr int kCtasPerSm = 2;      // resident CTAs per SM (shared memory: 4 stages x 24 KB)
 // Instruction descriptor of tcgen05.mma kind::f16: D fp32 (bits 4-5 = 1), A and B bf16 (bits 7-9 and
 // 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
@@ -52,7 +54,7 @@ struct Params {
   int y_f32;
   int M, N, K;
   int n_tiles, m_tiles, splits, kb_per_split, kb_total;
-  float* partial;      // [m_tiles * n_tiles][splits][BN / 4][BM][4]
+  float* partial;      // [m_tiles * n_tiles][BN / 4][BM][4] fp32 sums of the splits, zero between calls
   unsigned* counters;  // [m_tiles * n_tiles], zero between calls
   unsigned* err;
 };
@@ -97,6 +99,11 @@ MM_DEV bool wait_phase(unsigned long long* bar, unsigned parity) {
   return mbar_wait_parity_bounded(bar, parity, kWaitLimitNs);
 }
 
+MM_DEV void red_add_v4(float* p, float4 v) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
 MM_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 MM_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -131,7 +138,7 @@ MM_DEV void tc_ld32(uint32_t taddr, float (&v)[32]) {
 }
 MM_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-__global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) linear_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -243,12 +250,12 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
 
   const int tile = m_tile * p.n_tiles + n_tile;
   if (p.splits > 1) {
-    // Publish this split's partial ([BN / 4][BM][4] per split: a warp's 16-byte stores are contiguous), then
-    // count arrivals; the last CTA of the tile sums the splits in order.
-    float4* mine = reinterpret_cast<float4*>(p.partial + ((long long)tile * p.splits + split) * BM * BN);
+    // Add this split's partial into the tile's fp32 sum ([BN / 4][BM][4]: a warp's 16-byte reductions are
+    // contiguous), then count arrivals; the last CTA of the tile reads the sum, and zeroes it for the next call.
+    float* sum = p.partial + (long long)tile * BM * BN;
 #pragma unroll
     for (int q = 0; q < BN / 4; ++q)
-      __stcg(mine + q * BM + nl, make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]));
+      red_add_v4(sum + (q * BM + nl) * 4, make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]));
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -258,19 +265,17 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     __syncthreads();
     if (s.flag != 1) return;
     __threadfence();
+    float4* s4 = reinterpret_cast<float4*>(sum);
 #pragma unroll
-    for (int i = 0; i < BN; ++i) acc[i] = 0.f;
-    for (int sp = 0; sp < p.splits; ++sp) {
-      const float4* src = reinterpret_cast<const float4*>(p.partial + ((long long)tile * p.splits + sp) * BM * BN);
-#pragma unroll
-      for (int q = 0; q < BN / 4; ++q) {
-        const float4 v = __ldcg(src + q * BM + nl);
-        acc[4 * q] += v.x;
-        acc[4 * q + 1] += v.y;
-        acc[4 * q + 2] += v.z;
-        acc[4 * q + 3] += v.w;
-      }
+    for (int q = 0; q < BN / 4; ++q) {
+      const float4 v = __ldcg(s4 + q * BM + nl);
+      acc[4 * q] = v.x;
+      acc[4 * q + 1] = v.y;
+      acc[4 * q + 2] = v.z;
+      acc[4 * q + 3] = v.w;
     }
+#pragma unroll
+    for (int q = 0; q < BN / 4; ++q) __stcg(s4 + q * BM + nl, make_float4(0.f, 0.f, 0.f, 0.f));
     if (threadIdx.x == 0) p.counters[tile] = 0u;  // ready for the next call
   }
   if (n >= p.N) return;
@@ -347,9 +352,10 @@ static int make_plan(const MMLinearArgs* a, Plan* pl) {
   pl->kb_total = (int)((a->K + BK - 1) / BK);
   int splits = (int)a->splits;
   if (splits <= 0) {
-    // one wave of CTAs (one per SM), each streaming at least two K-blocks; at most kMaxSplits partials
+    // one wave of CTAs (kCtasPerSm per SM), each streaming at least two K-blocks; at most kMaxSplits
     const int ctas = pl->n_tiles * pl->m_tiles;
-    splits = ctas >= sm_count() ? 1 : std::min({sm_count() / ctas, pl->kb_total / 2, kMaxSplits});
+    const int wave = kCtasPerSm * sm_count();
+    splits = ctas >= wave ? 1 : std::min({wave / ctas, pl->kb_total / 2, kMaxSplits});
     splits = std::max(1, splits);
   }
   splits = std::min(splits, pl->kb_total);
@@ -362,7 +368,7 @@ static int make_plan(const MMLinearArgs* a, Plan* pl) {
   // partials (the counters must stay zero between calls).
   size_t off = 256 + kMaxTiles * sizeof(unsigned);
   pl->partial_off = off;
-  if (pl->splits > 1) off += tiles * pl->splits * BM * BN * sizeof(float);
+  if (pl->splits > 1) off += tiles * BM * BN * sizeof(float);
   pl->ws_bytes = off;
   return MM_OK;
 }
