@@ -335,26 +335,40 @@ struct StepParams {
   int silu;
 };
 
+#ifndef MM_CONV_STEP_ROWS
+#define MM_CONV_STEP_ROWS 2  // batch rows per thread in the conv decode step (the weights are reused across them)
+#endif
+constexpr int kStepRows = MM_CONV_STEP_ROWS;
+
 template <typename T>
 __global__ void __launch_bounds__(256) conv_step_kernel(const StepParams p) {
-  // grid (channel blocks, batch): no per-thread division
-  const int d = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+  // grid (channel blocks, batch / kStepRows): no per-thread division
+  const int d = blockIdx.x * blockDim.x + threadIdx.x, b0 = blockIdx.y * kStepRows;
   if (d >= p.dim) return;
-  const long long i = (long long)b * p.dim + d;
-  float4* st = reinterpret_cast<float4*>(p.state + i * kW);
-  // the window state first (with an early-state launch it loads while the kernel before this one
+  // the window states first (with an early-state launch they load while the kernel before this one
   // finishes); everything else after grid_dep_wait
-  const float4 s = *st;
+  float4 s[kStepRows];
+#pragma unroll
+  for (int r = 0; r < kStepRows; ++r)
+    if (b0 + r < p.batch) s[r] = *reinterpret_cast<const float4*>(p.state + ((long long)(b0 + r) * p.dim + d) * kW);
   grid_dep_wait();
   const float4 w = *reinterpret_cast<const float4*>(p.w + d * kW);
-  float v = p.bias ? p.bias[d] : 0.f;
-  const float xn = ld_f32(static_cast<const T*>(p.x) + b * p.xsb + d);
-  v = fmaf(w.x, s.y, v);
-  v = fmaf(w.y, s.z, v);
-  v = fmaf(w.z, s.w, v);
-  v = fmaf(w.w, xn, v);
-  *st = make_float4(s.y, s.z, s.w, xn);
-  st_f32(static_cast<T*>(p.out) + b * p.osb + d, act(v, p.silu));
+  const float bias = p.bias ? p.bias[d] : 0.f;
+  float xn[kStepRows];
+#pragma unroll
+  for (int r = 0; r < kStepRows; ++r)
+    xn[r] = b0 + r < p.batch ? ld_f32(static_cast<const T*>(p.x) + (long long)(b0 + r) * p.xsb + d) : 0.f;
+#pragma unroll
+  for (int r = 0; r < kStepRows; ++r) {
+    if (b0 + r >= p.batch) break;
+    float v = bias;
+    v = fmaf(w.x, s[r].y, v);
+    v = fmaf(w.y, s[r].z, v);
+    v = fmaf(w.z, s[r].w, v);
+    v = fmaf(w.w, xn[r], v);
+    *reinterpret_cast<float4*>(p.state + ((long long)(b0 + r) * p.dim + d) * kW) = make_float4(s[r].y, s[r].z, s[r].w, xn[r]);
+    st_f32(static_cast<T*>(p.out) + (long long)(b0 + r) * p.osb + d, act(v, p.silu));
+  }
 }
 
 }  // namespace conv
@@ -402,7 +416,7 @@ extern "C" int mm_causal_conv1d_step(const MMConvStepArgs* a, mm_stream_t stream
   p.silu = a->silu != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a->batch > 65535 || a->dim > (1 << 30)) return MM_ERR_SHAPE;  // grid.y = batch
-  const dim3 blocks((unsigned)((p.dim + 255) / 256), (unsigned)p.batch);
+  const dim3 blocks((unsigned)((p.dim + 255) / 256), (unsigned)((p.batch + conv::kStepRows - 1) / conv::kStepRows));
   cudaError_t e;
   if (a->dtype == MM_F32) e = launch_maybe_early(conv::conv_step_kernel<float>, blocks, 256, s, a->early_state, p);
   else if (a->dtype == MM_F16) e = launch_maybe_early(conv::conv_step_kernel<__half>, blocks, 256, s, a->early_state, p);
