@@ -206,6 +206,12 @@ __global__ void __launch_bounds__(1024) add_rmsnorm_kernel(const NormParams p) {
   const T* dl = p.delta ? static_cast<const T*>(p.delta) + (long long)r * p.dsr : nullptr;
   const int c0 = threadIdx.x * kNormE;
   float v[kNormE];
+  // the weights are loaded with the row, so that no load follows the block reduction
+  float4 wa = make_float4(0.f, 0.f, 0.f, 0.f), wb = wa;
+  if (VEC && c0 + kNormE <= p.dim) {
+    wa = *reinterpret_cast<const float4*>(p.w + c0);
+    wb = *reinterpret_cast<const float4*>(p.w + c0 + 4);
+  }
   if (VEC && c0 + kNormE <= p.dim) {
     const float4 a = *reinterpret_cast<const float4*>(res + c0);
     const float4 b = *reinterpret_cast<const float4*>(res + c0 + 4);
@@ -263,8 +269,6 @@ __global__ void __launch_bounds__(1024) add_rmsnorm_kernel(const NormParams p) {
   const float inv = rsqrtf(red[0] / (float)p.dim + p.eps);
   T* out = static_cast<T*>(p.out) + (long long)r * p.osr;
   if (VEC && c0 + kNormE <= p.dim) {
-    const float4 wa = *reinterpret_cast<const float4*>(p.w + c0);
-    const float4 wb = *reinterpret_cast<const float4*>(p.w + c0 + 4);
     const float w8[kNormE] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
     if (sizeof(T) == 2) {
       uint4 q;
