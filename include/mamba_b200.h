@@ -212,6 +212,16 @@ typedef struct MMSSMStepArgs {
   int64_t early_state; /* 1: ssm_state was not written by the kernel just before this call on `stream`, so
                           the call may start (and stream the state in) while that kernel finishes; every
                           other input is read after it completes (programmatic dependent launch) */
+  /* Optional fused dt projection (mamba_block.py:181, dt_proj(x_dbl[:, :dt_rank])): when dt_w != NULL
+     the call computes dt[b,d] = sum_k dt_in[b,k] * dt_w[d,k] + dt_bias[d] in fp32 (not rounded to
+     `dtype`) and does not read dt / dt_stride_b. dt_in: (batch, dt_rank) of `dtype`, unit inner stride,
+     row stride dt_in_stride_b (x_proj's first dt_rank output columns); dt_w: (dim, dt_rank) of `dtype`,
+     row stride dt_w_stride (dt_proj.weight); dt_bias: (dim,) fp32, may be NULL. dt_w, dt_bias and A are
+     read before the preceding kernel completes under early_state (they must not be its outputs). */
+  const void* dt_in;
+  const void* dt_w;
+  const float* dt_bias;
+  int64_t dt_rank, dt_in_stride_b, dt_w_stride;
 } MMSSMStepArgs;
 
 int mm_ssm_decode_step(const MMSSMStepArgs* args, mm_stream_t stream);

@@ -62,6 +62,8 @@ class MMSSMStepArgs(ctypes.Structure):
         ("y", _p), ("dtype", _i64), ("batch", _i64), ("dim", _i64), ("dstate", _i64),
         ("x_stride_b", _i64), ("dt_stride_b", _i64), ("z_stride_b", _i64), ("B_stride_b", _i64),
         ("C_stride_b", _i64), ("y_stride_b", _i64), ("dt_softplus", _i64), ("early_state", _i64),
+        ("dt_in", _p), ("dt_w", _p), ("dt_bias", _p), ("dt_rank", _i64), ("dt_in_stride_b", _i64),
+        ("dt_w_stride", _i64),
     ]
 
 

@@ -35,6 +35,15 @@ from mamba_metal_b200.selective_scan import selective_scan_into
 # B200 at configs[3] (batch 64) the cuBLAS projections are faster (53.5 vs 73.1 us per layer).
 USE_DECODE_GEMM = False
 DECODE_GEMM_MAX_ROWS = 256
+# With FUSED_DT_STEP, the decode step's dt_proj (a (batch, dt_rank) x (dt_rank, d_inner) product) runs inside
+# the SSM step kernel (a tensor-core tile per CTA) instead of as its own GEMM launch, for steps of at most
+# FUSED_DT_MAX_ELEMS (batch rows x channels of this rank). Off by default: measured on B200 with the 2.8b
+# shape (dt_rank 160, bf16, batch 64, CUDA graph), the whole decode step at 2 GPUs (2560 channels per rank)
+# is slower with it, 3.00 vs 2.80 ms per step, although two-kernel measurements (x_proj GEMM, then the step,
+# 64 layers) gave it 3.1-4.1 us per layer at 2560-640 channels x 64 rows (one wave of the fused kernel) and
+# nothing at 5120 x 64 (two waves: each CTA waits for its dt_proj rows and the MMA before its first state row).
+FUSED_DT_STEP = False
+FUSED_DT_MAX_ELEMS = 2560 * 64
 
 
 def decode_linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
@@ -96,13 +105,24 @@ class MambaBlock(nn.Module):
             self._A_cache = (key, (-torch.exp(self.A_log.float())).contiguous())
         return self._A_cache[1]
 
-    # dt_proj's bias in float32 for the decode GEMM's epilogue, cached until the parameter changes
+    # dt_proj's bias in float32 (the scan's delta_bias, the decode step's fused dt projection), cached until
+    # the parameter changes
     def _dt_bias32(self) -> torch.Tensor:
         b = self.dt_proj.bias
         key = (b.data_ptr(), b._version, b.device)
         if getattr(self, "_dt_bias_cache", None) is None or self._dt_bias_cache[0] != key:
             self._dt_bias_cache = (key, b.detach().float().contiguous())
         return self._dt_bias_cache[1]
+
+    def _fused_dt_step(self, batch: int) -> bool:
+        """The decode step computes dt_proj inside the SSM step kernel where that kernel's tensor-core dt tile
+        applies (16-bit weights, dt_rank a multiple of 16 up to ops.SSM_STEP_FUSED_DT_MAX_RANK, d_state 16,
+        d_inner a multiple of 8) and the step is small enough to gain (FUSED_DT_MAX_ELEMS); otherwise dt_proj
+        stays a separate GEMM."""
+        w = self.dt_proj.weight
+        return (FUSED_DT_STEP and w.dtype in (torch.float16, torch.bfloat16) and w.stride(1) == 1
+                and self.dt_rank % 16 == 0 and self.dt_rank <= ops.SSM_STEP_FUSED_DT_MAX_RANK
+                and self.d_state == 16 and self.d_inner % 8 == 0 and batch * self.d_inner <= FUSED_DT_MAX_ELEMS)
 
     def _run(self, x: torch.Tensor, want_state: bool):
         bsz, L, _ = x.shape
@@ -196,9 +216,15 @@ class MambaBlock(nn.Module):
                                     early_state=True)
         x_dbl = self._project(xc, self.x_proj.weight, 0)                    # (B, R + 2N)
         Df = self.D if self.D.dtype == torch.float32 else self.D.float()
-        dt = decode_linear(x_dbl[:, :R], self.dt_proj.weight, self.dt_proj.bias, bias32=self._dt_bias32())
-        y = ops.ssm_decode_step(xc, dt, xz[:, E:], x_dbl[:, R:R + N], x_dbl[:, R + N:], self._A(), Df,
-                                ssm_state, dt_softplus=True, early_state=True)
+        if self._fused_dt_step(xc.shape[0]):
+            # dt = dt_proj(x_dbl[:, :R]) computed inside the step kernel (fp32, bias included)
+            y = ops.ssm_decode_step(xc, None, xz[:, E:], x_dbl[:, R:R + N], x_dbl[:, R + N:], self._A(), Df,
+                                    ssm_state, dt_softplus=True, early_state=True, dt_in=x_dbl[:, :R],
+                                    dt_weight=self.dt_proj.weight, dt_bias=self._dt_bias32())
+        else:
+            dt = decode_linear(x_dbl[:, :R], self.dt_proj.weight, self.dt_proj.bias, bias32=self._dt_bias32())
+            y = ops.ssm_decode_step(xc, dt, xz[:, E:], x_dbl[:, R:R + N], x_dbl[:, R + N:], self._A(), Df,
+                                    ssm_state, dt_softplus=True, early_state=True)
         if defer_out and self.tp_reduce is not None and hasattr(self.tp_reduce, "partial"):
             # tensor parallel: leave out_proj's all-reduce to the caller's fused residual add + RMSNorm
             pending = self.tp_reduce.partial(y, self.out_proj.weight, self.tp_sites[1])

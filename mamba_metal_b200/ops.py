@@ -85,33 +85,53 @@ def causal_conv1d_step(x: torch.Tensor, conv_state: torch.Tensor, weight: torch.
     return out
 
 
+# Largest dt_rank whose fused dt projection runs in the dstate-16 step kernel (kDtMaxRank in mm_step.cu);
+# larger or odd ranks, and float32, take the one-thread-per-channel kernel.
+SSM_STEP_FUSED_DT_MAX_RANK = 160
+
+
 def ssm_decode_step(x, dt, z, B, C, A, D, ssm_state, *, dt_softplus: bool = True, out=None,
-                    early_state: bool = False) -> torch.Tensor:
+                    early_state: bool = False, dt_in=None, dt_weight=None, dt_bias=None) -> torch.Tensor:
     """One decode step of the SSM, updating ``ssm_state`` (float32 (batch, dim, dstate), contiguous) in
     place (mamba_block.py:183-195). x, dt, z: (batch, dim); B, C: (batch, dstate) (row strides free,
     unit inner stride); A: (dim, dstate) float32 contiguous; D: (dim,) float32 or None.
     ``early_state``: the caller guarantees that the kernel issued just before this call did not write
-    ``ssm_state``; the step then streams the state in while that kernel finishes."""
+    ``ssm_state``; the step then streams the state in while that kernel finishes.
+    With ``dt_weight`` (dt_proj.weight, (dim, dt_rank)) the step computes dt itself (mamba_block.py:181):
+    dt = dt_in @ dt_weight.T + dt_bias in float32, from ``dt_in`` (batch, dt_rank) (x_proj's first
+    dt_rank columns) and ``dt_bias`` ((dim,) float32 or None); ``dt`` is then not used (pass None)."""
     batch, dim = x.shape
     dstate = A.shape[1]
-    for t in (x, dt, z, B, C):
+    fused = dt_weight is not None
+    if fused:
+        assert dt_in is not None and dt_in.dim() == 2 and dt_in.shape[0] == batch
+        assert dt_weight.dim() == 2 and dt_weight.shape == (dim, dt_in.shape[1])
+        assert dt_bias is None or (dt_bias.shape == (dim,) and dt_bias.dtype == torch.float32
+                                   and dt_bias.is_contiguous())
+    else:
+        assert dt is not None
+    for t in (x, None if fused else dt, z, B, C, dt_in if fused else None, dt_weight):
         if t is not None:
             assert t.stride(-1) == 1 and t.dtype == x.dtype
     assert ssm_state.is_contiguous() and ssm_state.dtype == torch.float32
     assert A.is_contiguous() and A.dtype == torch.float32
-    dev = _lib.require_cuda(x, dt, z, B, C, A, D, ssm_state, out)
+    dev = _lib.require_cuda(x, dt, z, B, C, A, D, ssm_state, out, dt_in, dt_weight, dt_bias)
     if out is None:
         out = torch.empty((batch, dim), dtype=x.dtype, device=dev)
     a = _lib.MMSSMStepArgs()
-    a.x, a.dt, a.z, a.B, a.C, a.A, a.D = (_lib.ptr(t) for t in (x, dt, z, B, C, A, D))
+    a.x, a.dt, a.z, a.B, a.C, a.A, a.D = (_lib.ptr(t) for t in (x, None if fused else dt, z, B, C, A, D))
     a.ssm_state, a.y = ssm_state.data_ptr(), out.data_ptr()
     a.dtype = _lib.DTYPE_CODE[x.dtype]
     a.batch, a.dim, a.dstate = batch, dim, dstate
-    a.x_stride_b, a.dt_stride_b = x.stride(0), dt.stride(0)
+    a.x_stride_b = x.stride(0)
+    a.dt_stride_b = 0 if fused else dt.stride(0)
     a.z_stride_b = z.stride(0) if z is not None else 0
     a.B_stride_b, a.C_stride_b, a.y_stride_b = B.stride(0), C.stride(0), out.stride(0)
     a.dt_softplus = int(bool(dt_softplus))
     a.early_state = int(bool(early_state))
+    if fused:
+        a.dt_in, a.dt_w, a.dt_bias = _lib.ptr(dt_in), _lib.ptr(dt_weight), _lib.ptr(dt_bias)
+        a.dt_rank, a.dt_in_stride_b, a.dt_w_stride = dt_in.shape[1], dt_in.stride(0), dt_weight.stride(0)
     with torch.cuda.device(dev):
         rc = _lib.lib().mm_ssm_decode_step(ctypes.byref(a), _lib.stream_handle(dev))
     _lib.check(rc, "mm_ssm_decode_step")

@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
 def test_struct_layouts_are_padding_free():
     # all fields are 8 bytes wide, so sizeof == 8 * field count on every FFI
     for s, n in ((_lib.MMScanArgs, 9 + 5 + 6 * 3 + 2 + 3 + 1), (_lib.MMConvArgs, 5 + 4 + 1 + 6 + 1),
-                 (_lib.MMConvStepArgs, 5 + 1 + 3 + 2 + 1 + 1), (_lib.MMSSMStepArgs, 9 + 1 + 3 + 6 + 1 + 1),
+                 (_lib.MMConvStepArgs, 5 + 1 + 3 + 2 + 1 + 1), (_lib.MMSSMStepArgs, 9 + 1 + 3 + 6 + 1 + 1 + 3 + 3),
                  (_lib.MMAddNormArgs, 4 + 1 + 2 + 2 + 1)):
         assert ctypes.sizeof(s) == 8 * n, s.__name__
 
@@ -63,6 +63,8 @@ def test_conv_and_step_validation():
     assert lib.mm_causal_conv1d_fwd(ctypes.byref(c), None) == -1  # null pointers
     s = _lib.MMSSMStepArgs()
     s.dtype, s.batch, s.dim, s.dstate = 0, 1, 8, 65
+    assert lib.mm_ssm_decode_step(ctypes.byref(s), None) == -2
+    s.dstate, s.dt_w, s.dt_rank = 16, 16, 0  # fused dt projection (dt_w set, never dereferenced) without a rank
     assert lib.mm_ssm_decode_step(ctypes.byref(s), None) == -2
     r = _lib.MMAddNormArgs()
     r.dtype, r.rows, r.dim = 0, 1, 0

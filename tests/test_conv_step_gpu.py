@@ -94,6 +94,42 @@ def test_ssm_step_chain_matches_scan(dtype, n, b, d):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("b,d,rank,bias", [(64, 256, 160, True),   # the 2.8b shape's dt_rank (bf16 rows 320 B)
+                                           (9, 136, 48, True),     # the 130m dt_rank
+                                           (5, 64, 8, False),      # no bias
+                                           (3, 50, 48, True),      # dim % 8 != 0: one thread per channel
+                                           (4, 64, 12, True),      # rows not whole 16-byte chunks in 16-bit types
+                                           (4, 64, 200, True)])    # rows beyond the register-held limit
+def test_ssm_step_fused_dt_projection(dtype, b, d, rank, bias):
+    """dt = dt_in @ dt_w.T + dt_bias computed inside the step (mamba_block.py:181) equals the scan of the
+    same delta (float64 oracle) over a chain of steps; dt is never rounded to the element type."""
+    n, L = 16, 12
+    g = torch.Generator().manual_seed(rank * 7 + d)
+    inp = R.make_features_inputs(b, d, n, L, seed=rank)
+    qq = {k: (q(v, dtype) if k in ("u", "B", "C", "z") else v) for k, v in inp.items()}
+    dt_in = (torch.randn(b, rank, L, generator=g) * 0.5).to(dtype)
+    w = (torch.randn(d, rank, generator=g) / rank ** 0.5).to(dtype)
+    bvec = torch.randn(d, generator=g) - 2.0 if bias else None
+    delta = torch.einsum("bkl,dk->bdl", dt_in.double(), w.double())
+    if bias:
+        delta = delta + bvec.double()[None, :, None]
+    qq["delta"] = delta.numpy()
+    yr, hr = R.selective_scan_vec(**qq, delta_softplus=True, return_state=True, dtype=np.float64)
+    h = torch.zeros((b, d, n), device=DEV)
+    A = torch.as_tensor(inp["A"]).to(DEV)
+    D = torch.as_tensor(inp["D"]).to(DEV)
+    wd = w.to(DEV)
+    bd = bvec.to(DEV) if bias else None
+    gt = lambda k, t: torch.as_tensor(np.ascontiguousarray(qq[k][:, :, t])).to(DEV, dtype)
+    for t in range(L):
+        xin = dt_in[:, :, t].contiguous().to(DEV)
+        y = ssm_decode_step(gt("u", t), None, gt("z", t), gt("B", t), gt("C", t), A, D, h, dt_softplus=True,
+                            dt_in=xin, dt_weight=wd, dt_bias=bd)
+        assert_close(y, yr[:, :, t], RTOL[name(dtype)] * 2, f"t={t}")
+    assert_close(h, hr, 1e-4 if dtype == torch.float32 else 1e-2, "state")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("rows,dim", [(1, 768), (64, 2560), (7, 100)])
 def test_add_rmsnorm(dtype, rows, dim):
     g = torch.Generator().manual_seed(rows)

@@ -206,3 +206,29 @@ def test_config2_130m_prefill_and_greedy_decode():
     assert not mism.any(), f"greedy token mismatch at steps {torch.nonzero(mism).flatten().tolist()}"
     print(f"config2: steps 32-49 teacher-forced: {int((toks[0, 32:] != out[0, 32:]).sum())} differing tokens "
           f"(all at margins <= 1e-3)")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_step_fused_dt_matches_dt_gemm(dtype):
+    """MambaModel.step with dt_proj computed inside the SSM step kernel (mamba_block.FUSED_DT_STEP) against
+    dt_proj as a separate GEMM, from the same prefill state. The GEMM rounds dt to the model dtype and the
+    fused step does not, so the two agree to that dtype's accuracy (relative L2 <= 1e-2)."""
+    import mamba_metal_b200.mamba_block as mb
+
+    cfg = MambaConfig(d_model=256, n_layer=2, vocab_size=997, dt_rank=32)
+    m = init_weights_(MambaModel(cfg, dtype=dtype, device=DEV), seed=5)
+    ids = torch.randint(0, cfg.vocab_size, (6, 21), generator=torch.Generator().manual_seed(6)).to(DEV)
+    default = mb.FUSED_DT_STEP
+    outs = {}
+    try:
+        with torch.no_grad():
+            _, conv, ssm = m.prefill(ids)
+            for fused in (False, True):
+                mb.FUSED_DT_STEP = fused
+                assert m.layers[0].mixer._fused_dt_step(ids.shape[0]) == fused
+                logits, _, ssm2 = m.step(ids[:, -1:], [c.clone() for c in conv], [s.clone() for s in ssm])
+                outs[fused] = (logits.float(), ssm2[-1].clone())
+    finally:
+        mb.FUSED_DT_STEP = default
+    for a, b in zip(outs[True], outs[False]):
+        assert float((a - b).norm() / b.norm()) < 1e-2

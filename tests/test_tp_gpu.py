@@ -159,3 +159,60 @@ def test_peer_allreduce_exact():
     for p in procs:
         p.join(timeout=60)
     assert all(not r[1] for r in res), res
+
+
+def _fused_dt_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import mamba_metal_b200.mamba_block as mb
+    from mamba_metal_b200 import MambaConfig, MambaModel, init_weights_
+    from mamba_metal_b200.parallel import tp_model
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        cfg = MambaConfig(d_model=256, n_layer=2, vocab_size=997, dt_rank=16)
+        full = init_weights_(MambaModel(cfg, dtype=torch.bfloat16, device=dev), seed=7)
+        ids = torch.randint(0, cfg.vocab_size, (8, 29), generator=torch.Generator().manual_seed(4)).to(dev)
+        tp = tp_model(full, rank, world, peer_rows=64)
+        default = mb.FUSED_DT_STEP
+        mb.FUSED_DT_STEP = True
+        applies = all(layer.mixer._fused_dt_step(ids.shape[0]) for layer in tp.layers)
+        outs = {}
+        with torch.no_grad():
+            _, conv, ssm = tp.prefill(ids)
+            for fused in (False, True):
+                mb.FUSED_DT_STEP = fused
+                logits, _, ssm2 = tp.step(ids[:, -1:], [c.clone() for c in conv], [s.clone() for s in ssm])
+                outs[fused] = (logits.float(), ssm2[-1].clone())
+        mb.FUSED_DT_STEP = default
+        rel = lambda a, b: float((a - b).norm() / b.norm())
+        q.put((rank, applies, rel(outs[True][0], outs[False][0]), rel(outs[True][1], outs[False][1])))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, False, repr(e), None))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_fused_dt_step_matches_dt_gemm():
+    """bf16 tensor-parallel decode step: dt_proj computed inside the SSM step kernel (from the all-reduced
+    x_proj output and this rank's dt_proj rows) against dt_proj as a separate GEMM. The GEMM rounds dt to
+    bf16 and the fused step does not, so the two agree to bf16 accuracy (relative L2 <= 1e-2)."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_dt_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[1] is True and r[2] < 1e-2 and r[3] < 1e-2 for r in res), res
