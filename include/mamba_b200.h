@@ -21,7 +21,7 @@
  *   - mamba_metal/mamba_block.py:171-177 (decode: window shift, dot with the conv weight, + bias, SiLU).
  *     -> mm_causal_conv1d_step.
  *   - mamba_metal/mamba_block.py:183-195 (decode: softplus(dt), h = exp(dt*A)*h + dt*x*B,
- *     y = sum(h*C) + D*x, y *= silu(z)).
+ *     y = sum(h*C) + D*x, y *= silu(z)), and optionally the dt projection at :181.
  *     -> mm_ssm_decode_step.
  *   - mamba_metal/mamba_model.py:49-58 and :40,:69 (pre-RMSNorm + residual around each mixer).
  *     -> mm_add_rmsnorm.
@@ -216,8 +216,8 @@ typedef struct MMSSMStepArgs {
      the call computes dt[b,d] = sum_k dt_in[b,k] * dt_w[d,k] + dt_bias[d] in fp32 (not rounded to
      `dtype`) and does not read dt / dt_stride_b. dt_in: (batch, dt_rank) of `dtype`, unit inner stride,
      row stride dt_in_stride_b (x_proj's first dt_rank output columns); dt_w: (dim, dt_rank) of `dtype`,
-     row stride dt_w_stride (dt_proj.weight); dt_bias: (dim,) fp32, may be NULL. dt_w, dt_bias and A are
-     read before the preceding kernel completes under early_state (they must not be its outputs). */
+     row stride dt_w_stride (dt_proj.weight); dt_bias: (dim,) fp32, may be NULL. Under early_state dt_w and
+     dt_bias are read before the preceding kernel completes (they must not be its outputs). */
   const void* dt_in;
   const void* dt_w;
   const float* dt_bias;

@@ -148,15 +148,14 @@ __global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMPara
   constexpr int VE = 16 / sizeof(T);
   constexpr int kChunks = kQdCh / VE;  // 16-byte chunks per row slice
   const int tid = threadIdx.x, dl = tid >> 2, q = tid & 3;
-  const int bx_ = blockIdx.x, by_ = blockIdx.y;  // channel slice, row block
-  const int d0 = bx_ * kQdCh, d = d0 + dl;
+  const int d0 = blockIdx.x * kQdCh, d = d0 + dl;
   const bool dok = d < p.dim;
   // State rows first: with an early-state launch (programmatic dependent launch) they stream in while the
   // kernel before this one is still finishing; everything that kernel may have produced (dt, x, z, B, C,
   // dt_in) is read only after grid_dep_wait.
 #pragma unroll
   for (int g = 0; g < kQdGroups; ++g) {
-    const int b0 = (by_ * kQdGroups + g) * kQdRows;
+    const int b0 = ((int)blockIdx.y * kQdGroups + g) * kQdRows;
     const int nrows = max(0, min(kQdRows, p.batch - b0));
 #pragma unroll
     for (int r = 0; r < kQdRows; ++r)
@@ -178,13 +177,13 @@ __global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMPara
   }
   cp_async_commit();
   grid_dep_wait();
-  const int rows_cta = max(0, min(kQdGroups * kQdRows, p.batch - by_ * kQdGroups * kQdRows));
+  const int rows_cta = max(0, min(kQdGroups * kQdRows, p.batch - (int)blockIdx.y * kQdGroups * kQdRows));
   if (FDT) {  // dt_in rows of the whole CTA: their own commit group, ahead of the x / z slices
     const int dt_chunks = p.dt_rank / VE;
     for (int i = tid; i < rows_cta * dt_chunks; i += kQdThreads) {
       const int r = i / dt_chunks, c = i - r * dt_chunks;
       cp_async16(&sm.dtin[r][c * VE],
-                 static_cast<const T*>(p.dt_in) + (long long)(by_ * kQdGroups * kQdRows + r) * p.dtin_sb + c * VE);
+                 static_cast<const T*>(p.dt_in) + (long long)((int)blockIdx.y * kQdGroups * kQdRows + r) * p.dtin_sb + c * VE);
     }
     cp_async_commit();
   }
@@ -192,7 +191,7 @@ __global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMPara
   const float Dd = (dok && p.D) ? p.D[d] : 0.f;
 #pragma unroll
   for (int g = 0; g < kQdGroups; ++g) {
-    const int b0 = (by_ * kQdGroups + g) * kQdRows;
+    const int b0 = ((int)blockIdx.y * kQdGroups + g) * kQdRows;
     const int nrows = max(0, min(kQdRows, p.batch - b0));
     for (int i = FDT ? tid + kQdRows * kChunks : tid; i < 3 * kQdRows * kChunks; i += kQdThreads) {
       const int a = i / (kQdRows * kChunks), rem = i - a * kQdRows * kChunks;
@@ -207,7 +206,7 @@ __global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMPara
 #pragma unroll
   for (int j = 0; j < kQdGroups * kQdRows / 4; ++j) {
     const int gr = j * 4 + (tid >> 5), g = gr / kQdRows, r = gr - g * kQdRows, lane = tid & 31;
-    const int b = (by_ * kQdGroups + g) * kQdRows + r;
+    const int b = ((int)blockIdx.y * kQdGroups + g) * kQdRows + r;
     float v = 0.f;
     if (b < p.batch)
       v = lane < 16 ? ld_f32(static_cast<const T*>(p.B) + (long long)b * p.Bsb + lane)
@@ -240,7 +239,7 @@ __global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMPara
         }
       }
     }
-    const int b0 = (by_ * kQdGroups + g) * kQdRows;
+    const int b0 = ((int)blockIdx.y * kQdGroups + g) * kQdRows;
     const int nrows = max(0, min(kQdRows, p.batch - b0));
     if (!dok) continue;  // whole warps only (dim % 8 == 0, 8 channels per warp); no barrier follows
 #pragma unroll
