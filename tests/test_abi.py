@@ -81,3 +81,29 @@ def test_cpu_tensors_fail_loudly():
         selective_scan(u, u, torch.zeros(2, 4), torch.zeros(1, 4, 8), torch.zeros(1, 4, 8))
     with pytest.raises(AssertionError):
         selective_scan(u, torch.zeros(1, 2, 9), torch.zeros(2, 4), torch.zeros(1, 4, 8), torch.zeros(1, 4, 8))
+
+
+def test_ssm_step_fused_dt_argument_checks():
+    """Host-side checks of the fused dt projection arguments (ops.ssm_decode_step), which run before any
+    device work, and the loud failure on CPU tensors."""
+    import torch
+
+    from mamba_metal_b200 import ops
+
+    bf = torch.bfloat16
+    x = torch.zeros(2, 8, dtype=bf)
+    B = C = torch.zeros(2, 16, dtype=bf)
+    A, st = torch.zeros(8, 16), torch.zeros(2, 8, 16)
+    dt_in, w = torch.zeros(2, 16, dtype=bf), torch.zeros(8, 16, dtype=bf)
+    with pytest.raises(AssertionError):  # neither dt nor dt_weight
+        ops.ssm_decode_step(x, None, None, B, C, A, None, st)
+    with pytest.raises(AssertionError):  # dt_weight's rank differs from dt_in's
+        ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in, dt_weight=torch.zeros(8, 32, dtype=bf))
+    with pytest.raises(AssertionError):  # dt_weight rows must be the channels
+        ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in, dt_weight=torch.zeros(4, 16, dtype=bf))
+    with pytest.raises(AssertionError):  # the bias is float32
+        ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in, dt_weight=w, dt_bias=torch.zeros(8, dtype=bf))
+    with pytest.raises(AssertionError):  # dt_in of another dtype than x
+        ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in.float(), dt_weight=w)
+    with pytest.raises(RuntimeError, match="CUDA"):  # valid arguments, CPU tensors: no CPU path
+        ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in, dt_weight=w, dt_bias=torch.zeros(8))
