@@ -26,7 +26,7 @@ def test_struct_layouts_are_padding_free():
     # all fields are 8 bytes wide, so sizeof == 8 * field count on every FFI
     for s, n in ((_lib.MMScanArgs, 9 + 5 + 6 * 3 + 2 + 3 + 1), (_lib.MMConvArgs, 5 + 4 + 1 + 6 + 1),
                  (_lib.MMConvStepArgs, 5 + 1 + 3 + 2 + 1 + 1), (_lib.MMSSMStepArgs, 9 + 1 + 3 + 6 + 1 + 1 + 3 + 3),
-                 (_lib.MMAddNormArgs, 4 + 1 + 2 + 2 + 1)):
+                 (_lib.MMAddNormArgs, 4 + 1 + 2 + 2 + 1), (_lib.MMLinearArgs, 4 + 3 + 1 + 3 + 1)):
         assert ctypes.sizeof(s) == 8 * n, s.__name__
 
 
@@ -107,3 +107,30 @@ def test_ssm_step_fused_dt_argument_checks():
         ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in.float(), dt_weight=w)
     with pytest.raises(RuntimeError, match="CUDA"):  # valid arguments, CPU tensors: no CPU path
         ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in, dt_weight=w, dt_bias=torch.zeros(8))
+
+
+def test_linear_workspace_plan():
+    """mm_linear_workspace_size: the host-side plan of the small-batch GEMM (128-row weight tiles, 64-row
+    activation tiles, 64-wide K blocks): a fixed 256-byte header plus 4096 tile counters, and one fp32
+    128 x 64 partial tile per output tile when K is split. Without a device the SM count is taken as 148
+    (two CTAs each: a 296-CTA wave)."""
+    lib = _lib.lib()
+    head = 256 + 4096 * 4
+    tile = 128 * 64 * 4
+
+    def ws(M, N, K, splits, y_dtype=2):
+        a = _lib.MMLinearArgs()
+        a.M, a.N, a.K, a.splits, a.y_dtype = M, N, K, splits, y_dtype
+        n = ctypes.c_size_t(0)
+        rc = lib.mm_linear_workspace_size(ctypes.byref(a), ctypes.byref(n))
+        return rc, n.value
+
+    assert ws(64, 192, 5120, 1) == (0, head)                 # unsplit: no partial tiles
+    assert ws(64, 192, 5120, 4) == (0, head + 2 * tile)      # x_proj: 2 weight tiles x 1 batch tile, split
+    assert ws(64, 192, 64, 8) == (0, head)                   # one K block: the split is clamped to 1
+    assert ws(64 * 4097, 128, 5120, 4) == (0, head)          # more tiles than counter slots: not split
+    assert ws(64, 10240, 2560, 0) == (0, head + 80 * tile)   # in_proj, library's choice: 80 tiles split 3 ways
+    assert ws(64, 192, 5120, 0, y_dtype=0) == (0, head + 2 * tile)  # fp32 output, split up to 16 ways
+    assert ws(0, 192, 5120, 0)[0] == -2                      # empty shapes are refused
+    assert ws(64, 192, 5120, 0, y_dtype=1)[0] == -3          # fp16 output is not offered
+    assert lib.mm_linear_workspace_size(None, ctypes.byref(ctypes.c_size_t(0))) == -1
