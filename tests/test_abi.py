@@ -134,3 +134,38 @@ def test_linear_workspace_plan():
     assert ws(0, 192, 5120, 0)[0] == -2                      # empty shapes are refused
     assert ws(64, 192, 5120, 0, y_dtype=1)[0] == -3          # fp16 output is not offered
     assert lib.mm_linear_workspace_size(None, ctypes.byref(ctypes.c_size_t(0))) == -1
+
+
+def test_scan_work_plan():
+    """The scan's work plan, read back through mm_selective_scan_workspace_size: a 256-byte header, then
+    (each part 256-byte aligned) one 128-byte carry flag line, one aggregate (NM + 1 rows of 32 floats) and
+    one prefix (NM rows of 32 floats) per warp, so the size gives the warp count. Without a device the plan
+    targets 148 SMs x 3 CTAs x 4 warps = 1776 resident warps. Tiles are 32 bytes of time per row."""
+    lib = _lib.lib()
+
+    def a256(x):
+        return (x + 255) // 256 * 256
+
+    def size_for(n_warps, nm=16):
+        return 256 + a256(128 * max(n_warps, 1)) + a256(4 * n_warps * (nm + 1) * 32) + a256(4 * n_warps * nm * 32)
+
+    def ws(**kw):
+        a = _scan_args(piece_tiles=0)
+        for k, v in kw.items():
+            setattr(a, k, v)
+        n = ctypes.c_size_t(0)
+        assert lib.mm_selective_scan_workspace_size(ctypes.byref(a), ctypes.byref(n)) == 0
+        return n.value
+
+    # configs[1] (fp16 8 x 1536 x 4096): 98304 tiles in pieces of ceil(98304 / 1776) = 56 tiles, cut inside rows
+    assert ws(dtype=1, batch=8, dim=1536, seqlen=4096) == size_for(-(-98304 // 56))
+    # configs[3] prefill (bf16 64 x 5120 x 2048): 10240 rows >= 1776 warps, whole rows (6 x 128 tiles) per
+    # warp -- no carry hand-off -- since 768 tiles is within 9/8 of the split plan's 739
+    assert ws(dtype=2, batch=64, dim=5120, seqlen=2048) == size_for(-(-1310720 // 768))
+    # configs[2] prefill (fp32 1 x 1536 x 5601): rows of 701 tiles cut into pieces of 19 tiles (~37 per row)
+    assert ws(dtype=0, batch=1, dim=1536, seqlen=5601) == size_for(-(-33648 // 19))
+    # short sequences: pieces never shorter than two 32-step heads (4 fp16 tiles)
+    assert ws(dtype=1, batch=1, dim=64, seqlen=4096) == size_for(-(-512 // 4))
+    # an explicit piece length is kept, and dstate > 16 uses the 64-state layout
+    assert ws(dtype=1, batch=8, dim=1536, seqlen=4096, piece_tiles=256) == size_for(384)
+    assert ws(dtype=1, batch=2, dim=64, seqlen=1000, dstate=17, piece_tiles=4) == size_for(-(-252 // 4), nm=64)
