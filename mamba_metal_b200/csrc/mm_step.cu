@@ -177,13 +177,13 @@ __global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMPara
   }
   cp_async_commit();
   grid_dep_wait();
-  const int rows_cta = max(0, min(kQdGroups * kQdRows, p.batch - (int)blockIdx.y * kQdGroups * kQdRows));
+  const int row0 = (int)blockIdx.y * kQdGroups * kQdRows;  // the CTA's first batch row
+  const int rows_cta = max(0, min(kQdGroups * kQdRows, p.batch - row0));
   if (FDT) {  // dt_in rows of the whole CTA: their own commit group, ahead of the x / z slices
     const int dt_chunks = p.dt_rank / VE;
     for (int i = tid; i < rows_cta * dt_chunks; i += kQdThreads) {
       const int r = i / dt_chunks, c = i - r * dt_chunks;
-      cp_async16(&sm.dtin[r][c * VE],
-                 static_cast<const T*>(p.dt_in) + (long long)((int)blockIdx.y * kQdGroups * kQdRows + r) * p.dtin_sb + c * VE);
+      cp_async16(&sm.dtin[r][c * VE], static_cast<const T*>(p.dt_in) + (long long)(row0 + r) * p.dtin_sb + c * VE);
     }
     cp_async_commit();
   }
@@ -213,7 +213,8 @@ __global__ void __launch_bounds__(kQdThreads) ssm_step_quad_kernel(const SSMPara
                     : ld_f32(static_cast<const T*>(p.C) + (long long)b * p.Csb + (lane - 16));
     sm.bc[g][r][lane] = v;
   }
-  float dacc[4] = {0.f, 0.f, 0.f, 0.f};  // fused dt: accumulator fragment (rows lane / 4, channels 2 * (lane % 4) + {0, 1})
+  // fused dt: the MMA's accumulator fragment (batch rows lane / 4, channels 2 * (lane % 4) + {0, 1})
+  float dacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int g = 0; g < kQdGroups; ++g) {
     if (g == 0) cp_async_wait<kQdGroups - 1>();  // the state group, dt_in rows and group 0's row slices

@@ -102,7 +102,8 @@ def test_ssm_step_fused_dt_argument_checks():
     with pytest.raises(AssertionError):  # dt_weight rows must be the channels
         ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in, dt_weight=torch.zeros(4, 16, dtype=bf))
     with pytest.raises(AssertionError):  # the bias is float32
-        ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in, dt_weight=w, dt_bias=torch.zeros(8, dtype=bf))
+        ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in, dt_weight=w,
+                            dt_bias=torch.zeros(8, dtype=bf))
     with pytest.raises(AssertionError):  # dt_in of another dtype than x
         ops.ssm_decode_step(x, None, None, B, C, A, None, st, dt_in=dt_in.float(), dt_weight=w)
     with pytest.raises(RuntimeError, match="CUDA"):  # valid arguments, CPU tensors: no CPU path
