@@ -74,3 +74,32 @@ def test_reference_prefill_step_handoff():
         st, _, _ = ref.step(ids[:, L:L + 1], convs, ssms)
         full, _, _ = ref.prefill(ids[:, :L + 1])
         torch.testing.assert_close(st[:, 0], full[:, L], rtol=1e-4, atol=1e-4)
+
+
+def test_fused_dt_step_gate():
+    """Which decode steps compute dt_proj inside the SSM step kernel (MambaBlock._fused_dt_step): only with
+    FUSED_DT_STEP set, 16-bit weights, dt_rank a multiple of 16 up to the kernel's limit, d_state 16, and
+    at most FUSED_DT_MAX_ELEMS batch rows x channels; everything else keeps dt_proj as its own GEMM."""
+    import mamba_metal_b200.mamba_block as mb
+    from mamba_metal_b200 import MambaBlock, ops
+
+    def blk(d_model=256, dt_rank=32, d_state=16, dtype=torch.bfloat16):
+        with torch.device("meta"):
+            return MambaBlock(d_model, d_state=d_state, dt_rank=dt_rank, dtype=dtype)
+
+    default = mb.FUSED_DT_STEP
+    try:
+        mb.FUSED_DT_STEP = True
+        assert blk()._fused_dt_step(8)
+        assert blk(dtype=torch.float16)._fused_dt_step(8)
+        assert not blk(dtype=torch.float32)._fused_dt_step(8)             # fp32: separate GEMM
+        assert not blk(dt_rank=24)._fused_dt_step(8)                      # not a multiple of 16
+        assert not blk(dt_rank=ops.SSM_STEP_FUSED_DT_MAX_RANK + 16)._fused_dt_step(8)
+        assert not blk(d_state=8)._fused_dt_step(8)
+        b = blk(d_model=2560, dt_rank=160)                                 # 2.8b mixer, 5120 channels
+        assert b._fused_dt_step(mb.FUSED_DT_MAX_ELEMS // 5120)
+        assert not b._fused_dt_step(mb.FUSED_DT_MAX_ELEMS // 5120 + 1)   # beyond the size limit
+        mb.FUSED_DT_STEP = False
+        assert not blk()._fused_dt_step(8)
+    finally:
+        mb.FUSED_DT_STEP = default
